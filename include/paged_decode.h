@@ -1,0 +1,156 @@
+/* paged_decode.h — C ABI of the B200 (sm_100a) paged split-K GQA decode operator.
+ *
+ * Drop-in boundary for ensigncode/paged-decode-lab.  The reference binds one
+ * pybind entry, ext.decode(q, k, v, table, lengths, numerator, stats, out,
+ * split_tokens, merge_mode) (src/paged_decode/csrc/bindings.cpp:9 ->
+ * decode_cuda, src/paged_decode/csrc/decode.cu:197-246), behind the Python
+ * DecodePlan (src/paged_decode/runtime.py:23-90).  This header splits that
+ * into a host-side plan (built once from CPU metadata, like DecodePlan.__init__)
+ * and an allocation-free decode call (like DecodePlan.run).  Only plain C
+ * types cross it: no torch types, no exceptions; every call returns a
+ * pd_status and pd_last_error() gives the message.
+ *
+ * Layouts (as in the reference, decode.cu:59-60):
+ *   q      [batch, query_heads, head_dim]                 float16 | float32
+ *   k, v   [physical_pages, page_size, kv_heads, head_dim] same dtype as q
+ *   table  [batch, table_width] int32, -1 allowed past each row's live pages
+ *   lengths[batch] int32
+ *   out    [batch, query_heads, head_dim] float32
+ * Query head h reads KV head h / (query_heads / kv_heads); scores are scaled
+ * by 1/sqrt(head_dim); an empty sequence yields a zero row.
+ *
+ * Device memory is owned by the caller: pd_plan_device_bytes() says how many
+ * bytes one plan needs (metadata + split-K workspace), the caller allocates
+ * them (cudaMalloc, a torch tensor, ...) and hands them to pd_plan_bind().
+ * pd_decode() allocates nothing, never synchronises and may be captured in a
+ * CUDA graph.  A plan may be used on one stream at a time.
+ */
+#ifndef PAGED_DECODE_B200_H
+#define PAGED_DECODE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PD_ABI_VERSION 1
+
+typedef enum pd_status {
+    PD_OK = 0,
+    PD_ERR_VALUE = 1,        /* bad shape, limit, pointer or state (Python: ValueError)  */
+    PD_ERR_TYPE = 2,         /* unsupported dtype (Python: TypeError)                    */
+    PD_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed (Python: RuntimeError) */
+    PD_ERR_DEVICE = 4,       /* a kernel raised its error word (Python: RuntimeError)    */
+    PD_ERR_UNBOUND = 5       /* plan has no device buffer yet (Python: RuntimeError)     */
+} pd_status;
+
+typedef enum pd_dtype { PD_FLOAT16 = 0, PD_FLOAT32 = 1 } pd_dtype;
+
+/* Error-word bits a kernel can raise (read with pd_plan_read_errors). */
+#define PD_DEVERR_TIMEOUT 1u      /* a bounded wait on a shared-memory barrier ran out */
+#define PD_DEVERR_BAD_PAGE 2u     /* a live page id outside [0, physical_pages): tokens skipped */
+
+/* Replaces oracle.Layout (src/paged_decode/oracle.py:11-27). */
+typedef struct pd_layout {
+    int32_t batch;
+    int32_t query_heads;
+    int32_t kv_heads;
+    int32_t head_dim;        /* 64 or 128 */
+    int32_t page_size;       /* 16 or 32  */
+    int64_t physical_pages;
+} pd_layout;
+
+typedef struct pd_plan pd_plan;
+
+typedef struct pd_plan_info {
+    int32_t splits;          /* max(1, ceil(max_context / split_tokens)), runtime.py:49 */
+    int32_t max_context;     /* max(lengths) */
+    int32_t num_ctas;        /* persistent CTAs the decode kernel launches */
+    int32_t num_segments;    /* (group, page range) work segments over all CTAs */
+    int32_t num_groups;      /* (sequence, KV head, query-head tile) groups */
+    int32_t num_pieces;      /* segments of groups that span >1 CTA: partials to merge */
+    int32_t group_tile;      /* query heads per group tile (8, 16 or 32) */
+    int32_t total_pages;     /* page tiles streamed per decode (all groups) */
+    int64_t workspace_bytes; /* split-K partials + merge counters */
+    int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
+} pd_plan_info;
+
+/* Build a plan from host metadata.  Replaces DecodePlan.__init__'s checks and
+ * split planning (runtime.py:32-69) and decode_cuda's validation
+ * (decode.cu:201-237).  Copies table and lengths.  merge_mode 0 = "serial",
+ * 1 = "shared" is accepted for API compatibility (runtime.py:33-34); the
+ * kernel always uses its fused merge.  device < 0 builds a host-only plan
+ * (inspection, no decode).  num_ctas <= 0 picks one CTA per SM of device.
+ */
+pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                         const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
+                         int32_t device, int32_t num_ctas, pd_plan **out_plan);
+
+void pd_plan_destroy(pd_plan *plan);
+
+pd_status pd_plan_get_info(const pd_plan *plan, pd_plan_info *info);
+
+/* Work list, for inspection and tests: segments as int32 quadruples
+ * (group, first_page, end_page, piece or -1), groups as int32 octuples
+ * (batch, kv_head, first_query_head, query_heads, length, first_piece, pieces, 0)
+ * and per-CTA segment offsets [num_ctas + 1].  Any pointer may be NULL.
+ */
+pd_status pd_plan_copy_worklist(const pd_plan *plan, int32_t *segments, int32_t *groups,
+                                int32_t *cta_offsets);
+
+size_t pd_plan_device_bytes(const pd_plan *plan);
+
+/* Give the plan its device buffer (>= pd_plan_device_bytes, 256-byte aligned,
+ * on the plan's device) and upload metadata on `stream` (a cudaStream_t; NULL
+ * = legacy default stream).  Synchronises that stream.  May be called again
+ * to move the plan to a new buffer or to clear its error word and counters.
+ */
+pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *stream);
+
+/* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
+ * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
+ * k and v must be 16-byte aligned (TMA).  Asynchronous on `stream`.
+ */
+pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
+                    float *out, void *stream);
+
+/* As pd_decode, and also writes stats[batch, query_heads, 2] = (m, l): the
+ * running maximum of score*log2(e)/sqrt(head_dim) and the softmax denominator
+ * relative to it (m = -inf, l = 0 for an empty sequence).  Used by sequence
+ * sharding: each GPU decodes its page range, then pd_merge_shards combines.
+ * No reference counterpart (the reference never ran on more than one GPU).
+ */
+pd_status pd_decode_with_stats(pd_plan *plan, const void *q, const void *k, const void *v,
+                               pd_dtype dtype, float *out, float *stats, void *stream);
+
+/* Max-corrected merge of per-shard results (the merge algebra of
+ * oracle.py:88-96 applied across shards): shard_out [shards, rows, head_dim]
+ * and shard_stats [shards, rows, 2] as written by pd_decode_with_stats,
+ * out [rows, head_dim].  Device pointers on the current device.
+ */
+pd_status pd_merge_shards(const float *shard_out, const float *shard_stats, int32_t shards,
+                          int64_t rows, int32_t head_dim, float *out, void *stream);
+
+/* Debug gather through the decode kernel's own TMA page path: writes the
+ * live K and V rows of every (sequence, KV head) as dense
+ * [batch, kv_heads, max_context, head_dim] arrays in the input dtype
+ * (rows past a sequence's length are left untouched).  Bit-exact with
+ * oracle.gather_cache (oracle.py:50-56) by construction; used by the tests.
+ */
+pd_status pd_gather_debug(pd_plan *plan, const void *k, const void *v, pd_dtype dtype,
+                          void *dense_k, void *dense_v, void *stream);
+
+/* Copy the device error word to *error_word and clear it (synchronises `stream`). */
+pd_status pd_plan_read_errors(pd_plan *plan, uint32_t *error_word, void *stream);
+
+const char *pd_status_string(pd_status status);
+const char *pd_last_error(void);     /* message of this thread's last failing call */
+int32_t pd_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_DECODE_B200_H */

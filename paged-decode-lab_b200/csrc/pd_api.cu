@@ -1,0 +1,365 @@
+// pd_api.cu — C ABI of the decode operator: plans, TMA descriptors, launches.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <new>
+#include <set>
+#include <string>
+#include <type_traits>
+#include <utility>
+
+#include "pd_decode_kernel.cuh"
+#include "pd_plan.hpp"
+
+#define PD_API extern "C" __attribute__((visibility("default")))
+
+namespace pd {
+const std::string &last_error();
+
+namespace {
+
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const DecodeArgs);
+
+struct KernelEntry {
+    KernelFn fn;
+    int threads;
+    size_t smem;
+};
+
+// Consumer warps per CTA and ring slots: 8 consumers (4 when 32 query heads
+// share a KV head, whose accumulators need 128 registers per thread) and a
+// ~128 KiB ring of page tiles.
+template <typename Elt, int D, int T, int GT, int MODE>
+KernelEntry make_entry() {
+    constexpr int NC = GT == 32 ? 4 : 8;
+    constexpr int TILE = 2 * T * D * int(sizeof(Elt));
+    constexpr int SL0 = 131072 / TILE;
+    constexpr int SLOTS = SL0 < 2 ? 2 : (SL0 > 32 ? 32 : SL0);
+    using S = KernelShape<Elt, D, T, GT, NC, SLOTS>;
+    return {&paged_decode_kernel<Elt, D, T, GT, NC, SLOTS, MODE>, S::THREADS, S::SMEM};
+}
+
+template <typename Elt, int D, int T, int MODE>
+KernelEntry entry_gt(int gt) {
+    if (MODE == kModeGather || gt == 8) return make_entry<Elt, D, T, 8, MODE>();
+    if (gt == 16) return make_entry<Elt, D, T, 16, MODE>();
+    return make_entry<Elt, D, T, 32, MODE>();
+}
+
+template <typename Elt, int MODE>
+KernelEntry entry_dt(int D, int T, int gt) {
+    if (D == 64) return T == 16 ? entry_gt<Elt, 64, 16, MODE>(gt) : entry_gt<Elt, 64, 32, MODE>(gt);
+    return T == 16 ? entry_gt<Elt, 128, 16, MODE>(gt) : entry_gt<Elt, 128, 32, MODE>(gt);
+}
+
+KernelEntry kernel_for(pd_dtype dtype, int D, int T, int gt, int mode) {
+    if (dtype == PD_FLOAT16)
+        return mode == kModeDecode ? entry_dt<__half, kModeDecode>(D, T, gt)
+                                   : entry_dt<__half, kModeGather>(D, T, gt);
+    return mode == kModeDecode ? entry_dt<float, kModeDecode>(D, T, gt)
+                               : entry_dt<float, kModeGather>(D, T, gt);
+}
+
+std::mutex g_attr_mutex;
+std::set<std::pair<int, KernelFn>> g_attr_done;
+
+pd_status ensure_smem_attribute(int device, const KernelEntry &e) {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (g_attr_done.count({device, e.fn})) return PD_OK;
+    const cudaError_t err = cudaFuncSetAttribute(reinterpret_cast<const void *>(e.fn),
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(e.smem));
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(err));
+    g_attr_done.insert({device, e.fn});
+    return PD_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) ==
+                cudaSuccess &&
+            query == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// K or V cache [P, T, Hkv, D] viewed as 3-D {D, Hkv, P*T}: one box = the T
+// token rows of one page for one KV head, 128 bytes of head dims wide.
+pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, CUtensorMap *map) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const int elt = dtype == PD_FLOAT16 ? 2 : 4;
+    const pd_layout &L = p.layout;
+    cuuint64_t dims[3] = {cuuint64_t(L.head_dim), cuuint64_t(L.kv_heads),
+                          cuuint64_t(L.physical_pages) * cuuint64_t(L.page_size)};
+    cuuint64_t strides[2] = {cuuint64_t(L.head_dim) * elt, cuuint64_t(L.kv_heads) * L.head_dim * elt};
+    cuuint32_t box[3] = {cuuint32_t(128 / elt), 1, cuuint32_t(L.page_size)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode(map,
+                              dtype == PD_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              3, const_cast<void *>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    return PD_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != device) err = cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0 && err == cudaSuccess) cudaSetDevice(prev);
+    }
+};
+
+pd_status check_bound(const pd_plan *p) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (p->device < 0) return fail(PD_ERR_VALUE, "host-only plan (device < 0) cannot launch");
+    if (!p->dev) return fail(PD_ERR_UNBOUND, "plan has no device buffer: call pd_plan_bind first");
+    return PD_OK;
+}
+
+pd_status check_dtype(pd_dtype dtype) {
+    if (dtype != PD_FLOAT16 && dtype != PD_FLOAT32)
+        return fail(PD_ERR_TYPE, "q/k/v must share float16 or float32 dtype");
+    return PD_OK;
+}
+
+DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
+    DecodeArgs a{};
+    uint8_t *dev = p->dev;
+    const DeviceImage &im = p->image;
+    a.q = q;
+    a.table = reinterpret_cast<const int32_t *>(dev + im.off_table);
+    a.cta_off = reinterpret_cast<const int32_t *>(dev + im.off_cta);
+    a.segs = reinterpret_cast<const int4 *>(dev + im.off_segs);
+    a.groups = reinterpret_cast<const int4 *>(dev + im.off_groups);
+    a.counters = reinterpret_cast<int32_t *>(dev + im.off_counters);
+    a.part_o = reinterpret_cast<float *>(dev + im.off_part_o);
+    a.part_ml = reinterpret_cast<float2 *>(dev + im.off_part_ml);
+    a.out = out;
+    a.stats = stats;
+    a.error = reinterpret_cast<uint32_t *>(dev + im.off_error);
+    a.Hq = p->layout.query_heads;
+    a.Hkv = p->layout.kv_heads;
+    a.W = int32_t(p->width);
+    a.max_len = p->max_context;
+    a.P = p->layout.physical_pages;
+    a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
+    return a;
+}
+
+pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int mode,
+                 const DecodeArgs &args, void *stream) {
+    if (!k || !v) return fail(PD_ERR_VALUE, "k and v must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
+        return fail(PD_ERR_VALUE, "k and v must be 16-byte aligned");
+    TensorMapCache &tc = p->tmaps;
+    if (tc.k != k || tc.v != v || tc.dtype != int(dtype)) {
+        pd_status s = encode_cache_map(*p, k, dtype, &tc.map_k);
+        if (s != PD_OK) return s;
+        s = encode_cache_map(*p, v, dtype, &tc.map_v);
+        if (s != PD_OK) return s;
+        tc.k = k;
+        tc.v = v;
+        tc.dtype = int(dtype);
+    }
+    const KernelEntry e = kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, mode);
+    pd_status s = ensure_smem_attribute(p->device, e);
+    if (s != PD_OK) return s;
+    e.fn<<<p->num_ctas, e.threads, e.smem, static_cast<cudaStream_t>(stream)>>>(tc.map_k, tc.map_v,
+                                                                              args);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
+pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
+                      float *out, float *stats, void *stream) {
+    pd_status s = check_bound(p);
+    if (s != PD_OK) return s;
+    if ((s = check_dtype(dtype)) != PD_OK) return s;
+    if (!q || !out) return fail(PD_ERR_VALUE, "q and out must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return fail(PD_ERR_VALUE, "q and out must be 16-byte aligned");
+    if (stats && (reinterpret_cast<uintptr_t>(stats) & 7))
+        return fail(PD_ERR_VALUE, "stats must be 8-byte aligned");
+    DeviceGuard guard(p->device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    const DecodeArgs args = make_args(p, q, out, stats);
+    return launch(p, k, v, dtype, kModeDecode, args, stream);
+}
+
+}  // namespace
+}  // namespace pd
+
+using namespace pd;
+
+PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                                const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
+                                int32_t device, int32_t num_ctas, pd_plan **out_plan) {
+    if (!out_plan) return fail(PD_ERR_VALUE, "out_plan must not be NULL");
+    *out_plan = nullptr;
+    int sm_count = 148;
+    if (device >= 0) {
+        const cudaError_t err = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
+        if (err != cudaSuccess)
+            return fail(PD_ERR_CUDA, std::string("device query: ") + cudaGetErrorString(err));
+    }
+    pd_plan *p = new (std::nothrow) pd_plan();
+    if (!p) return fail(PD_ERR_VALUE, "out of host memory");
+    const pd_status s =
+        build_plan(layout, table, table_width, lengths, split_tokens, merge_mode, num_ctas, sm_count, *p);
+    if (s != PD_OK) {
+        delete p;
+        return s;
+    }
+    p->device = device;
+    *out_plan = p;
+    return PD_OK;
+}
+
+PD_API void pd_plan_destroy(pd_plan *plan) { delete plan; }
+
+PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
+    if (!p || !info) return fail(PD_ERR_VALUE, "plan and info must not be NULL");
+    info->splits = p->splits;
+    info->max_context = p->max_context;
+    info->num_ctas = p->num_ctas;
+    info->num_segments = int32_t(p->segs.size() / 4);
+    info->num_groups = int32_t(p->groups.size() / 8);
+    info->num_pieces = p->num_pieces;
+    info->group_tile = p->group_tile;
+    info->total_pages = int32_t(p->total_pages);
+    info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o) +
+                            int64_t(p->groups.size() / 8) * 4;
+    info->device_bytes = int64_t(p->image.bytes);
+    return PD_OK;
+}
+
+PD_API pd_status pd_plan_copy_worklist(const pd_plan *p, int32_t *segments, int32_t *groups,
+                                       int32_t *cta_offsets) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (segments) std::copy(p->segs.begin(), p->segs.end(), segments);
+    if (groups) std::copy(p->groups.begin(), p->groups.end(), groups);
+    if (cta_offsets) std::copy(p->cta_off.begin(), p->cta_off.end(), cta_offsets);
+    return PD_OK;
+}
+
+PD_API size_t pd_plan_device_bytes(const pd_plan *p) { return p ? p->image.bytes : 0; }
+
+PD_API pd_status pd_plan_bind(pd_plan *p, void *buffer, size_t bytes, void *stream) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (p->device < 0) return fail(PD_ERR_VALUE, "host-only plan (device < 0) cannot be bound");
+    if (!buffer || bytes < p->image.bytes)
+        return fail(PD_ERR_VALUE, "device buffer is NULL or smaller than pd_plan_device_bytes()");
+    if (reinterpret_cast<uintptr_t>(buffer) & 255)
+        return fail(PD_ERR_VALUE, "device buffer must be 256-byte aligned");
+    DeviceGuard guard(p->device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    auto st = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaMemcpyAsync(buffer, p->host_image.data(), p->host_image.size(),
+                                      cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("plan upload: ") + cudaGetErrorString(err));
+    p->dev = static_cast<uint8_t *>(buffer);
+    p->dev_bytes = bytes;
+    return PD_OK;
+}
+
+PD_API pd_status pd_decode(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
+                           float *out, void *stream) {
+    return decode_impl(p, q, k, v, dtype, out, nullptr, stream);
+}
+
+PD_API pd_status pd_decode_with_stats(pd_plan *p, const void *q, const void *k, const void *v,
+                                      pd_dtype dtype, float *out, float *stats, void *stream) {
+    if (!stats) return fail(PD_ERR_VALUE, "stats must not be NULL");
+    return decode_impl(p, q, k, v, dtype, out, stats, stream);
+}
+
+PD_API pd_status pd_merge_shards(const float *shard_out, const float *shard_stats, int32_t shards,
+                                 int64_t rows, int32_t head_dim, float *out, void *stream) {
+    if (!shard_out || !shard_stats || !out) return fail(PD_ERR_VALUE, "pointers must not be NULL");
+    if (shards < 1 || rows < 0 || head_dim <= 0)
+        return fail(PD_ERR_VALUE, "shards >= 1, rows >= 0 and head_dim > 0 required");
+    if (rows == 0) return PD_OK;
+    constexpr int kRowsPerBlock = 8;
+    const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+    if (blocks > INT32_MAX) return fail(PD_ERR_VALUE, "too many rows");
+    merge_shards_kernel<<<unsigned(blocks), kRowsPerBlock * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        shard_out, reinterpret_cast<const float2 *>(shard_stats), shards, rows, head_dim, out);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
+PD_API pd_status pd_gather_debug(pd_plan *p, const void *k, const void *v, pd_dtype dtype,
+                                 void *dense_k, void *dense_v, void *stream) {
+    pd_status s = check_bound(p);
+    if (s != PD_OK) return s;
+    if ((s = check_dtype(dtype)) != PD_OK) return s;
+    if (!dense_k || !dense_v) return fail(PD_ERR_VALUE, "dense outputs must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(dense_k) | reinterpret_cast<uintptr_t>(dense_v)) & 15)
+        return fail(PD_ERR_VALUE, "dense outputs must be 16-byte aligned");
+    DeviceGuard guard(p->device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    DecodeArgs args = make_args(p, nullptr, nullptr, nullptr);
+    args.dense_k = dense_k;
+    args.dense_v = dense_v;
+    return launch(p, k, v, dtype, kModeGather, args, stream);
+}
+
+PD_API pd_status pd_plan_read_errors(pd_plan *p, uint32_t *error_word, void *stream) {
+    pd_status s = check_bound(p);
+    if (s != PD_OK) return s;
+    if (!error_word) return fail(PD_ERR_VALUE, "error_word must not be NULL");
+    DeviceGuard guard(p->device);
+    auto st = static_cast<cudaStream_t>(stream);
+    uint32_t word = 0;
+    cudaError_t err = cudaMemcpyAsync(&word, p->dev + p->image.off_error, 4, cudaMemcpyDeviceToHost, st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(p->dev + p->image.off_error, 0, 4, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("error word read: ") + cudaGetErrorString(err));
+    *error_word = word;
+    return PD_OK;
+}
+
+PD_API const char *pd_status_string(pd_status status) {
+    switch (status) {
+        case PD_OK: return "ok";
+        case PD_ERR_VALUE: return "invalid value";
+        case PD_ERR_TYPE: return "invalid dtype";
+        case PD_ERR_CUDA: return "CUDA error";
+        case PD_ERR_DEVICE: return "device error word set";
+        case PD_ERR_UNBOUND: return "plan not bound to a device buffer";
+    }
+    return "unknown status";
+}
+
+PD_API const char *pd_last_error(void) { return pd::last_error().c_str(); }
+
+PD_API int32_t pd_abi_version(void) { return PD_ABI_VERSION; }

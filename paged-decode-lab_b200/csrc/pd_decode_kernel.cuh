@@ -1,0 +1,687 @@
+// pd_decode_kernel.cuh — persistent paged split-K GQA decode kernel for sm_100a.
+//
+// Replaces the reference's partial_decode + merge_decode/merge_shared
+// (src/paged_decode/csrc/decode.cu:26-168) with one persistent kernel:
+//
+//   * one CTA per SM walks a host-built list of segments; a segment is a run
+//     of logical pages of one group = (sequence, KV head, query-head tile);
+//     the host balances pages across CTAs, so every SM streams the same bytes;
+//   * warp NC (producer) looks up each page in the page table and gathers its
+//     K and V rows for the segment's KV head with 3-D tiled TMA loads
+//     (128-byte swizzle, no multicast) into a ring of shared-memory slots,
+//     completion tracked by mbarriers;
+//   * warps 0..NC-1 (consumers) take the ring's tiles round-robin and fold
+//     them into a per-warp online softmax (running max m, denominator l,
+//     unnormalised output o) for all G query heads of the KV head at once:
+//     FP16 inputs use m16n8k16 tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T,
+//     FP32 accumulators), FP32 inputs use FP32 FMAs;
+//   * at a segment's end the consumer warps combine their states through
+//     shared memory; a group owned by one CTA writes its normalised output
+//     directly, otherwise each CTA writes an (m, l, o) partial and the CTA
+//     that arrives last (atomic counter, reset after use) merges them.
+//
+// All exponentials are base 2 on scores pre-multiplied by log2(e)/sqrt(D);
+// this is the reference's exp(s - m) rewritten, not a different softmax.
+#pragma once
+
+#include <type_traits>
+
+#include "pd_device.cuh"
+
+namespace pd {
+
+struct DecodeArgs {
+    const void *q;            // [B, Hq, D] in the input dtype
+    const int32_t *table;     // [B, W]
+    const int32_t *cta_off;   // [C + 1] segment range of each CTA
+    const int4 *segs;         // {group, first_page, end_page, piece (-1: sole piece)}
+    const int4 *groups;       // 2 per group: {b, kvh, h0, nh}, {length, piece0, npieces, 0}
+    int32_t *counters;        // [groups] arrivals of multi-piece groups (self-resetting)
+    float *part_o;            // [pieces, GT, D] unnormalised partial outputs
+    float2 *part_ml;          // [pieces, GT] (m, l) of each partial
+    float *out;               // [B, Hq, D]
+    float *stats;             // [B, Hq, 2] (m, l) or nullptr
+    uint32_t *error;          // error word (PD_DEVERR_* bits)
+    void *dense_k;            // gather mode: [B, Hkv, max_len, D]
+    void *dense_v;
+    int32_t Hq, Hkv, W, max_len;
+    int64_t P;
+    float scale_log2;         // log2(e) / sqrt(D)
+};
+
+constexpr uint32_t kErrTimeout = 1u;
+constexpr uint32_t kErrBadPage = 2u;
+
+template <typename Elt, int D, int T, int GT, int NC, int SLOTS>
+struct KernelShape {
+    static constexpr int ELT = sizeof(Elt);
+    static constexpr int ROW_BYTES = D * ELT;
+    static constexpr int NBOX = ROW_BYTES / 128;       // 128-byte TMA boxes per token row
+    static constexpr int BOX_ELEMS = 128 / ELT;
+    static constexpr int HALF_BYTES = T * ROW_BYTES;   // K (or V) part of one page tile
+    static constexpr int TILE_BYTES = 2 * HALF_BYTES;
+    static constexpr int OSTRIDE = D + 4;              // padded merge rows: conflict-free stores
+    static constexpr int THREADS = (NC + 1) * 32;
+    static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
+    static constexpr size_t MERGE_O = size_t(NC) * GT * OSTRIDE * 4;
+    static constexpr size_t MERGE_ML = size_t(NC) * GT * 2 * 4;
+    static constexpr size_t QS = size_t(GT) * D * ELT;
+    static constexpr size_t BARS = size_t(SLOTS) * 16;
+    static constexpr size_t FLAGS = size_t(SLOTS) * 4 + 16;
+    static constexpr size_t SMEM = 1024 + RING + MERGE_O + MERGE_ML + QS + BARS + FLAGS;
+    static_assert(ROW_BYTES % 128 == 0, "token rows must be whole 128-byte boxes");
+    static_assert(HALF_BYTES % 1024 == 0, "tiles must keep 1024-byte swizzle alignment");
+    static_assert(SMEM <= 232448, "shared memory budget exceeded");
+};
+
+struct SmemFlags {
+    volatile int abort;
+    int last;
+    int pad[2];
+};
+
+// ------------------------------------------------------------------ FP16 tensor-core engine
+// One warp's online-softmax state for all GT query heads of a KV head.
+// S^T[t][g] = K[t][:] . Q[g][:]  with A = K tile (ldmatrix), B = Q^T fragments;
+// O^T[d][g] += V^T[d][t] P^T[t][g] with A = V tile (ldmatrix.trans), B = P^T,
+// where P^T comes from the S^T accumulators by movmatrix.trans (no shared memory).
+template <int D, int T, int GT>
+struct HalfEngine {
+    static constexpr int NT = GT / 8;    // n-tiles of 8 query heads
+    static constexpr int KS = D / 16;    // k-steps of the QK^T product
+    static constexpr int DT = D / 16;    // m-tiles of the PV product (head dims)
+    static constexpr int MT = T / 16;    // 16-token m-tiles per page
+    static constexpr bool Q_REGS = NT <= 2;
+
+    uint32_t qf[Q_REGS ? KS : 1][Q_REGS ? NT : 1][2];
+    float acc[DT][NT][4];
+    float m[NT][2], l[NT][2];
+    uint32_t qs;     // Q tile in shared memory (Q_REGS == false), row-swizzled
+    int lane;
+
+    // Q^T fragment: b0 = Q[g][d0..d0+1], b1 = Q[g][d0+8..d0+9], g = nt*8 + lane/4.
+    __device__ __forceinline__ void begin(const __half *qrow, int nh, int lane_, uint32_t qs_) {
+        lane = lane_;
+        qs = qs_;
+        if constexpr (Q_REGS) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int g = nt * 8 + (lane >> 2);
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int d0 = ks * 16 + 2 * (lane & 3);
+                    uint32_t lo = 0, hi = 0;
+                    if (g < nh) {
+                        const uint32_t *src = reinterpret_cast<const uint32_t *>(qrow + g * D + d0);
+                        lo = src[0];
+                        hi = src[4];
+                    }
+                    qf[ks][nt][0] = lo;
+                    qf[ks][nt][1] = hi;
+                }
+            }
+        }
+#pragma unroll
+        for (int dt = 0; dt < DT; ++dt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[dt][nt][i] = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m[nt][0] = m[nt][1] = -INFINITY;
+            l[nt][0] = l[nt][1] = 0.f;
+        }
+    }
+
+    __device__ __forceinline__ void q_frag(int ks, int nt, uint32_t &b0, uint32_t &b1) const {
+        if constexpr (Q_REGS) {
+            b0 = qf[ks][nt][0];
+            b1 = qf[ks][nt][1];
+        } else {
+            // rows g of 2*D bytes; 16-byte chunk c of row g stored at chunk (c ^ (g & 7)).
+            uint32_t r[2];
+            const int sub = (lane >> 3) & 1;     // lanes 0-7: chunk 2ks, lanes 8-15: chunk 2ks+1
+            const int g = nt * 8 + (lane & 7);
+            const int c = ks * 2 + sub;
+            const uint32_t addr = qs + g * (D * 2) + (((c & 8) | ((c & 7) ^ (g & 7))) << 4);
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+                         : "=r"(r[0]), "=r"(r[1])
+                         : "r"(addr));
+            b0 = r[0];
+            b1 = r[1];
+        }
+    }
+
+    __device__ __forceinline__ void tile(uint32_t kbase, int valid, float scale_log2) {
+        const uint32_t vbase = kbase + T * D * 2;
+        const int mi = lane >> 3, r8 = lane & 7;
+        float x[MT][NT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) x[mt][nt][i] = 0.f;
+            const int row = mt * 16 + r8 + (mi & 1) * 8;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t a[4];
+                ldmatrix_x4(a, kbase + swz128<T>(row, ks * 2 + (mi >> 1)));
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    uint32_t b0, b1;
+                    q_frag(ks, nt, b0, b1);
+                    mma_16816(x[mt][nt], a, b0, b1);
+                }
+            }
+        }
+        // scale into log2 units and mask tokens past the sequence end
+        const bool full = valid >= T;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int tok = mt * 16 + (lane >> 2) + ((i & 2) ? 8 : 0);
+                    float v = x[mt][nt][i] * scale_log2;
+                    if (!full && tok >= valid) v = -INFINITY;
+                    x[mt][nt][i] = v;
+                }
+        uint32_t pb[MT][NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                mx0 = fmaxf(mx0, fmaxf(x[mt][nt][0], x[mt][nt][2]));
+                mx1 = fmaxf(mx1, fmaxf(x[mt][nt][1], x[mt][nt][3]));
+            }
+#pragma unroll
+            for (int s = 4; s < 32; s <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(kFullMask, mx0, s));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(kFullMask, mx1, s));
+            }
+            const float n0 = fmaxf(m[nt][0], mx0), n1 = fmaxf(m[nt][1], mx1);
+            const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
+            const float a0 = exp2f(m[nt][0] - u0), a1 = exp2f(m[nt][1] - u1);
+            m[nt][0] = n0;
+            m[nt][1] = n1;
+            l[nt][0] *= a0;
+            l[nt][1] *= a1;
+#pragma unroll
+            for (int dt = 0; dt < DT; ++dt) {
+                acc[dt][nt][0] *= a0;
+                acc[dt][nt][1] *= a1;
+                acc[dt][nt][2] *= a0;
+                acc[dt][nt][3] *= a1;
+            }
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                // The weights enter the MMA as FP16; l sums the same rounded
+                // weights so that o / l stays an exact convex combination.
+                const uint32_t p01 = pack_half2(exp2f(x[mt][nt][0] - u0), exp2f(x[mt][nt][1] - u1));
+                const uint32_t p23 = pack_half2(exp2f(x[mt][nt][2] - u0), exp2f(x[mt][nt][3] - u1));
+                const float2 f01 = unpack_half2(p01), f23 = unpack_half2(p23);
+                l[nt][0] += f01.x + f23.x;
+                l[nt][1] += f01.y + f23.y;
+                pb[mt][nt][0] = movmatrix_trans(p01);
+                pb[mt][nt][1] = movmatrix_trans(p23);
+            }
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const int row = mt * 16 + r8 + (mi >> 1) * 8;
+#pragma unroll
+            for (int dt = 0; dt < DT; ++dt) {
+                uint32_t a[4];
+                ldmatrix_x4_trans(a, vbase + swz128<T>(row, dt * 2 + (mi & 1)));
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma_16816(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
+            }
+        }
+    }
+
+    // Publish (m, l, o) of this warp to the merge buffers.
+    __device__ __forceinline__ void store(float *sm_m, float *sm_l, float *sm_o) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int s = 4; s < 32; s <<= 1) l[nt][i] += __shfl_xor_sync(kFullMask, l[nt][i], s);
+        if (lane < 4) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int g = nt * 8 + 2 * lane + i;
+                    sm_m[g] = m[nt][i];
+                    sm_l[g] = l[nt][i];
+                }
+        }
+        constexpr int OS = D + 4;
+#pragma unroll
+        for (int dt = 0; dt < DT; ++dt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int g = nt * 8 + 2 * (lane & 3);
+                const int d = dt * 16 + (lane >> 2);
+                sm_o[g * OS + d] = acc[dt][nt][0];
+                sm_o[(g + 1) * OS + d] = acc[dt][nt][1];
+                sm_o[g * OS + d + 8] = acc[dt][nt][2];
+                sm_o[(g + 1) * OS + d + 8] = acc[dt][nt][3];
+            }
+    }
+};
+
+// ------------------------------------------------------------------ FP32 engine
+// Lanes own tokens for the scores (one row of K per lane, Q broadcast from
+// shared memory) and own head dims for the value sum.
+template <int D, int T, int GT>
+struct FloatEngine {
+    static constexpr int DPL = D / 32;           // value dims per lane
+    static constexpr int HALVES = 32 / T;        // lanes per token in the score phase
+    static constexpr int CHUNKS = D / 4 / HALVES;  // float4 chunks of K per lane
+
+    float acc[GT][DPL];
+    float m[GT], l[GT];
+    uint32_t qs;
+    int nh, lane;
+
+    __device__ __forceinline__ void begin(int nh_, int lane_, uint32_t qs_) {
+        nh = nh_;
+        lane = lane_;
+        qs = qs_;
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+            m[g] = -INFINITY;
+            l[g] = 0.f;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
+        }
+    }
+
+    __device__ __forceinline__ void tile(uint32_t kbase, int valid, float scale_log2) {
+        const uint32_t vbase = kbase + T * D * 4;
+        const int t = lane % T;
+        const int half = lane / T;
+        float x[GT];
+#pragma unroll
+        for (int g = 0; g < GT; ++g) x[g] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < CHUNKS; ++c) {
+            const int chunk = half * CHUNKS + c;
+            const float4 kv = lds_f4(kbase + swz128<T>(t, chunk));
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+                if (g < nh) {
+                    const float4 qv = lds_f4(qs + (g * D + chunk * 4) * 4);
+                    x[g] = fmaf(qv.x, kv.x, x[g]);
+                    x[g] = fmaf(qv.y, kv.y, x[g]);
+                    x[g] = fmaf(qv.z, kv.z, x[g]);
+                    x[g] = fmaf(qv.w, kv.w, x[g]);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+            if (g < nh) {
+                float s = x[g];
+                if (HALVES == 2) s += __shfl_xor_sync(kFullMask, s, 16);
+                s = t < valid ? s * scale_log2 : -INFINITY;
+                float mx = s;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
+                const float nm = fmaxf(m[g], mx);
+                const float u = nm == -INFINITY ? 0.f : nm;
+                const float alpha = exp2f(m[g] - u);
+                m[g] = nm;
+                const float p = exp2f(s - u);
+                l[g] = l[g] * alpha + (half == 0 ? p : 0.f);
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[g][i] *= alpha;
+                x[g] = p;
+            }
+        }
+#pragma unroll 4
+        for (int tt = 0; tt < T; ++tt) {
+            float vv[DPL];
+            if constexpr (DPL == 2) {
+                const float2 v2 = lds_f2(vbase + swz128<T>(tt, lane >> 1) + (lane & 1) * 8);
+                vv[0] = v2.x;
+                vv[1] = v2.y;
+            } else {
+                const float4 v4 = lds_f4(vbase + swz128<T>(tt, lane));
+                vv[0] = v4.x;
+                vv[1] = v4.y;
+                vv[2] = v4.z;
+                vv[3] = v4.w;
+            }
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+                if (g < nh) {
+                    const float p = __shfl_sync(kFullMask, x[g], tt);
+#pragma unroll
+                    for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
+                }
+            }
+        }
+    }
+
+    __device__ __forceinline__ void store(float *sm_m, float *sm_l, float *sm_o) {
+        constexpr int OS = D + 4;
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+            float s = l[g];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) s += __shfl_xor_sync(kFullMask, s, o);
+            if (lane == 0) {
+                sm_m[g] = m[g];
+                sm_l[g] = s;
+            }
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) sm_o[g * OS + lane * DPL + i] = acc[g][i];
+        }
+    }
+};
+
+template <typename Elt, int D, int T, int GT>
+struct EngineFor;
+template <int D, int T, int GT>
+struct EngineFor<__half, D, T, GT> {
+    using type = HalfEngine<D, T, GT>;
+};
+template <int D, int T, int GT>
+struct EngineFor<float, D, T, GT> {
+    using type = FloatEngine<D, T, GT>;
+};
+
+// ------------------------------------------------------------------ kernel
+enum : int { kModeDecode = 0, kModeGather = 1 };
+
+template <typename Elt, int D, int T, int GT, int NC, int SLOTS, int MODE>
+__global__ void __launch_bounds__((NC + 1) * 32, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
+    using S = KernelShape<Elt, D, T, GT, NC, SLOTS>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem;
+    float *merge_o = reinterpret_cast<float *>(ring + S::RING);
+    float *merge_m = merge_o + size_t(NC) * GT * S::OSTRIDE;
+    float *merge_l = merge_m + size_t(NC) * GT;
+    uint8_t *qsm = reinterpret_cast<uint8_t *>(merge_l + size_t(NC) * GT);
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(qsm + S::QS);
+    uint64_t *empty_bar = full_bar + SLOTS;
+    int *slot_valid = reinterpret_cast<int *>(empty_bar + SLOTS);
+    SmemFlags *flags = reinterpret_cast<SmemFlags *>(slot_valid + SLOTS);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int seg_begin = a.cta_off[blockIdx.x];
+    const int seg_end = a.cta_off[blockIdx.x + 1];
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SLOTS; ++s) {
+            mbar_init(smem_u32(full_bar + s), 1);
+            mbar_init(smem_u32(empty_bar + s), 1);
+        }
+        flags->abort = 0;
+        flags->last = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    if (warp == NC) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_descriptor(&tm_k);
+            tma_prefetch_descriptor(&tm_v);
+        }
+        bool stop = false;
+        int j = 0;
+        for (int si = seg_begin; si < seg_end; ++si) {
+            const int4 sg = a.segs[si];
+            const int4 g0 = a.groups[2 * sg.x];
+            const int32_t *trow = a.table + int64_t(g0.x) * a.W;
+            const int kvh = g0.y;
+            for (int pg = sg.y; pg < sg.z; pg += 32) {
+                const int n = min(32, sg.z - pg);
+                const int mine = lane < n ? __ldg(trow + pg + lane) : 0;
+                for (int i = 0; i < n; ++i, ++j) {
+                    const int page = __shfl_sync(kFullMask, mine, i);
+                    if (lane == 0 && !stop) {
+                        const int slot = j % SLOTS;
+                        const int use = j / SLOTS;
+                        const uint32_t fb = smem_u32(full_bar + slot);
+                        if (flags->abort ||
+                            (use > 0 && !mbar_wait(smem_u32(empty_bar + slot), (use - 1) & 1))) {
+                            if (!flags->abort) atomicOr(a.error, kErrTimeout);
+                            flags->abort = 1;
+                            stop = true;
+                        } else if (page >= 0 && int64_t(page) < a.P) {
+                            slot_valid[slot] = 1;
+                            mbar_arrive_expect_tx(fb, S::TILE_BYTES);
+                            const uint32_t dst = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+#pragma unroll
+                            for (int bx = 0; bx < S::NBOX; ++bx)
+                                tma_load_3d(dst + bx * T * 128, &tm_k, bx * S::BOX_ELEMS, kvh, page * T, fb);
+#pragma unroll
+                            for (int bx = 0; bx < S::NBOX; ++bx)
+                                tma_load_3d(dst + S::HALF_BYTES + bx * T * 128, &tm_v, bx * S::BOX_ELEMS,
+                                            kvh, page * T, fb);
+                        } else {
+                            // The reference skips tokens whose page id is out of range
+                            // (decode.cu:58); plans validate ids, so this is defence only.
+                            atomicOr(a.error, kErrBadPage);
+                            slot_valid[slot] = 0;
+                            mbar_arrive(fb);
+                        }
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    constexpr int CT = NC * 32;
+    const int ctid = threadIdx.x;
+    bool stop = false;
+    int j = 0;
+    for (int si = seg_begin; si < seg_end; ++si) {
+        const int4 sg = a.segs[si];
+        const int4 g0 = a.groups[2 * sg.x];
+        const int4 g1 = a.groups[2 * sg.x + 1];
+        const int b = g0.x, kvh = g0.y, h0 = g0.z, nh = g0.w;
+        const int length = g1.x;
+        const int npg = sg.z - sg.y;
+        const int first = ((warp - j) % NC + NC) % NC;
+
+        if constexpr (MODE == kModeGather) {
+            constexpr int CPR = S::ROW_BYTES / 16;   // 16-byte chunks per token row
+            for (int t = first; t < npg; t += NC) {
+                const int jj = j + t;
+                const int slot = jj % SLOTS;
+                if (!stop && !flags->abort) {
+                    if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
+                        if (lane == 0) atomicOr(a.error, kErrTimeout);
+                        flags->abort = 1;
+                        stop = true;
+                    } else {
+                        const int lp = sg.y + t;
+                        const int valid = min(T, length - lp * T);
+                        if (slot_valid[slot]) {
+                            const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+                            const int64_t base = (int64_t(b) * a.Hkv + kvh) * a.max_len + int64_t(lp) * T;
+                            for (int idx = lane; idx < valid * CPR; idx += 32) {
+                                const int r = idx / CPR, c = idx % CPR;
+                                const float4 kv = lds_f4(kb + swz128<T>(r, c));
+                                const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<T>(r, c));
+                                const int64_t off = (base + r) * S::ROW_BYTES + c * 16;
+                                *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_k) + off) = kv;
+                                *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_v) + off) = vv;
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(empty_bar + slot));
+                    }
+                }
+            }
+            j += npg;
+            continue;
+        } else {
+            using Engine = typename EngineFor<Elt, D, T, GT>::type;
+            Engine eng;
+            const Elt *qrow = static_cast<const Elt *>(a.q) + (int64_t(b) * a.Hq + h0) * D;
+            const uint32_t qs = smem_u32(qsm);
+            constexpr bool kQsmem = !std::is_same<Elt, __half>::value || !HalfEngine<D, T, GT>::Q_REGS;
+            if constexpr (kQsmem) {
+                // cooperative Q tile load (zero rows for heads past nh)
+                if constexpr (std::is_same<Elt, float>::value) {
+                    float *qf = reinterpret_cast<float *>(qsm);
+                    for (int e = ctid; e < GT * D; e += CT) {
+                        const int g = e / D;
+                        qf[e] = g < nh ? qrow[e] : 0.f;
+                    }
+                } else {
+                    for (int e = ctid; e < GT * (D / 8); e += CT) {
+                        const int g = e / (D / 8), c = e % (D / 8);
+                        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (g < nh) v = *reinterpret_cast<const float4 *>(qrow + g * D + c * 8);
+                        const int sc = (c & 8) | ((c & 7) ^ (g & 7));
+                        *reinterpret_cast<float4 *>(qsm + g * D * 2 + sc * 16) = v;
+                    }
+                }
+                named_barrier_sync(1, CT);
+            }
+            if constexpr (std::is_same<Elt, __half>::value)
+                eng.begin(reinterpret_cast<const __half *>(qrow), nh, lane, qs);
+            else
+                eng.begin(nh, lane, qs);
+
+            for (int t = first; t < npg; t += NC) {
+                const int jj = j + t;
+                const int slot = jj % SLOTS;
+                if (stop || flags->abort) break;
+                if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
+                    if (lane == 0) atomicOr(a.error, kErrTimeout);
+                    flags->abort = 1;
+                    stop = true;
+                    break;
+                }
+                if (slot_valid[slot]) {
+                    const int lp = sg.y + t;
+                    eng.tile(smem_u32(ring + size_t(slot) * S::TILE_BYTES), min(T, length - lp * T),
+                             a.scale_log2);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(empty_bar + slot));
+            }
+            j += npg;
+
+            // ---------------------------------------------------- combine warps
+            eng.store(merge_m + warp * GT, merge_l + warp * GT, merge_o + size_t(warp) * GT * S::OSTRIDE);
+            named_barrier_sync(1, CT);
+            const int piece = sg.w;
+            for (int e = ctid; e < nh * D; e += CT) {
+                const int g = e / D, d = e - g * D;
+                float top = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < NC; ++w)
+                    if (merge_l[w * GT + g] > 0.f) top = fmaxf(top, merge_m[w * GT + g]);
+                float den = 0.f, num = 0.f;
+#pragma unroll
+                for (int w = 0; w < NC; ++w) {
+                    const float lw = merge_l[w * GT + g];
+                    if (lw > 0.f) {
+                        const float f = exp2f(merge_m[w * GT + g] - top);
+                        den = fmaf(f, lw, den);
+                        num = fmaf(f, merge_o[(w * GT + g) * S::OSTRIDE + d], num);
+                    }
+                }
+                if (piece < 0) {
+                    const int64_t row = int64_t(b) * a.Hq + h0 + g;
+                    a.out[row * D + d] = den > 0.f ? num / den : 0.f;
+                    if (a.stats && d == 0)
+                        reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
+                } else {
+                    a.part_o[(int64_t(piece) * GT + g) * D + d] = num;
+                    if (d == 0) a.part_ml[int64_t(piece) * GT + g] = make_float2(top, den);
+                }
+            }
+            if (piece >= 0) {
+                // last-arriving CTA of the group merges all its partials
+                __threadfence();
+                named_barrier_sync(1, CT);
+                if (ctid == 0) {
+                    const int prev = atomicAdd(a.counters + sg.x, 1);
+                    flags->last = (prev == g1.z - 1);
+                }
+                named_barrier_sync(1, CT);
+                if (flags->last) {
+                    __threadfence();
+                    const int p0 = g1.y, np = g1.z;
+                    for (int e = ctid; e < nh * D; e += CT) {
+                        const int g = e / D, d = e - g * D;
+                        float top = -INFINITY;
+                        for (int p = 0; p < np; ++p) {
+                            const float2 ml = __ldcg(a.part_ml + int64_t(p0 + p) * GT + g);
+                            if (ml.y > 0.f) top = fmaxf(top, ml.x);
+                        }
+                        float den = 0.f, num = 0.f;
+                        for (int p = 0; p < np; ++p) {
+                            const float2 ml = __ldcg(a.part_ml + int64_t(p0 + p) * GT + g);
+                            if (ml.y > 0.f) {
+                                const float f = exp2f(ml.x - top);
+                                den = fmaf(f, ml.y, den);
+                                num = fmaf(f, __ldcg(a.part_o + (int64_t(p0 + p) * GT + g) * D + d), num);
+                            }
+                        }
+                        const int64_t row = int64_t(b) * a.Hq + h0 + g;
+                        a.out[row * D + d] = den > 0.f ? num / den : 0.f;
+                        if (a.stats && d == 0)
+                            reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
+                    }
+                    if (ctid == 0) a.counters[sg.x] = 0;
+                }
+            }
+            named_barrier_sync(1, CT);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ cross-shard merge
+// out[row] = sum_s exp2(m_s - M) * l_s * o_s / sum_s exp2(m_s - M) * l_s over shards
+// with l_s > 0 (o_s is each shard's normalised output); zero when all are empty.
+__global__ void merge_shards_kernel(const float *__restrict__ shard_out,
+                                    const float2 *__restrict__ shard_stats, int shards, int64_t rows,
+                                    int D, float *__restrict__ out) {
+    const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float top = -INFINITY;
+    for (int s = 0; s < shards; ++s) {
+        const float2 ml = shard_stats[int64_t(s) * rows + row];
+        if (ml.y > 0.f) top = fmaxf(top, ml.x);
+    }
+    float den = 0.f;
+    for (int s = 0; s < shards; ++s) {
+        const float2 ml = shard_stats[int64_t(s) * rows + row];
+        if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
+    }
+    for (int d = lane; d < D; d += 32) {
+        float num = 0.f;
+        for (int s = 0; s < shards; ++s) {
+            const float2 ml = shard_stats[int64_t(s) * rows + row];
+            if (ml.y > 0.f)
+                num = fmaf(exp2f(ml.x - top) * ml.y, shard_out[(int64_t(s) * rows + row) * D + d], num);
+        }
+        out[row * D + d] = den > 0.f ? num / den : 0.f;
+    }
+}
+
+}  // namespace pd

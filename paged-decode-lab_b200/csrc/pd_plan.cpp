@@ -1,0 +1,202 @@
+// pd_plan.cpp — plan builder: validation, balanced page partition, device image.
+//
+// The reference plans a rectangular grid [Hq, B, splits] sized by the longest
+// sequence (runtime.py:49, decode.cu:176).  Here the unit of work is a page
+// tile of one group = (sequence, KV head, query-head tile): all G query heads
+// of a KV head share every K/V byte they read.  The total page count over all
+// groups is cut into num_ctas equal contiguous ranges, so each persistent CTA
+// (one per SM) streams the same number of bytes, ragged batches included.
+// A group cut by a range boundary yields one partial per piece; the kernel's
+// last-arriving CTA merges them with the max-corrected merge.
+#include "pd_plan.hpp"
+
+#include <algorithm>
+#include <climits>
+#include <cstring>
+
+namespace pd {
+
+namespace {
+thread_local std::string g_last_error;
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+}  // namespace
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+
+pd_status fail(pd_status status, const std::string &msg) {
+    g_last_error = msg;
+    return status;
+}
+
+const std::string &last_error() { return g_last_error; }
+
+pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
+                     const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
+                     int32_t num_ctas, int32_t sm_count, pd_plan &p) {
+    if (!layout) return fail(PD_ERR_VALUE, "layout must not be NULL");
+    const pd_layout L = *layout;
+    // Layout.__post_init__ (oracle.py:24-27)
+    if (L.batch <= 0 || L.query_heads <= 0 || L.kv_heads <= 0 || L.head_dim <= 0 ||
+        L.page_size <= 0 || L.physical_pages <= 0)
+        return fail(PD_ERR_VALUE, "layout dimensions must be positive");
+    if (L.query_heads % L.kv_heads)
+        return fail(PD_ERR_VALUE, "query_heads must be divisible by kv_heads");
+    // DecodePlan limits (runtime.py:33-42)
+    if (merge_mode != 0 && merge_mode != 1)
+        return fail(PD_ERR_VALUE, "merge must be 'serial' or 'shared'");
+    if (L.head_dim != 64 && L.head_dim != 128)
+        return fail(PD_ERR_VALUE, "head_dim must be 64 or 128");
+    if (L.page_size != 16 && L.page_size != 32)
+        return fail(PD_ERR_VALUE, "page_size must be 16 or 32");
+    if (L.batch > 65535 || L.query_heads > 65535)
+        return fail(PD_ERR_VALUE, "batch/head count exceeds CUDA grid limits");
+    if (split_tokens < 1 || split_tokens > 1048576)
+        return fail(PD_ERR_VALUE, "split_tokens must be an integer in [1,1048576]");
+    // validate_metadata (oracle.py:30-47)
+    if (width < 0) return fail(PD_ERR_VALUE, "page table must have shape [batch, logical_pages]");
+    if (!lengths || (width > 0 && !table))
+        return fail(PD_ERR_VALUE, "table and lengths must not be NULL");
+    const int64_t capacity = width * L.page_size;
+    for (int b = 0; b < L.batch; ++b)
+        if (lengths[b] < 0 || lengths[b] > capacity)
+            return fail(PD_ERR_VALUE, "sequence length exceeds page table capacity");
+    if (std::max<int64_t>(width, L.physical_pages) > INT32_MAX)
+        return fail(PD_ERR_VALUE, "metadata exceeds int32 addressing limits");
+    for (int b = 0; b < L.batch; ++b) {
+        const int64_t live = (int64_t(lengths[b]) + L.page_size - 1) / L.page_size;
+        for (int64_t i = 0; i < live; ++i) {
+            const int32_t page = table[b * width + i];
+            if (page < 0 || page >= L.physical_pages)
+                return fail(PD_ERR_VALUE, "live logical page maps outside physical cache");
+        }
+    }
+    if (width > 65536) return fail(PD_ERR_VALUE, "page table width must not exceed 65536");
+    int32_t max_context = 0;
+    for (int b = 0; b < L.batch; ++b) max_context = std::max(max_context, lengths[b]);
+    if (max_context > 1048576)
+        return fail(PD_ERR_VALUE, "this implementation supports at most 1M context tokens");
+    const int64_t splits = std::max<int64_t>(1, (int64_t(max_context) + split_tokens - 1) / split_tokens);
+    if (splits > 65535) return fail(PD_ERR_VALUE, "too many context splits");
+    // TMA row coordinates are int32: page * page_size must fit.
+    if (L.physical_pages * L.page_size > INT32_MAX)
+        return fail(PD_ERR_VALUE, "physical_pages * page_size exceeds int32 TMA coordinates");
+
+    p.layout = L;
+    p.width = width;
+    p.split_tokens = split_tokens;
+    p.merge_mode = merge_mode;
+    p.splits = int32_t(splits);
+    p.max_context = max_context;
+    p.group = L.query_heads / L.kv_heads;
+    p.group_tile = p.group <= 8 ? 8 : (p.group <= 16 ? 16 : 32);
+    p.group_splits = (p.group + p.group_tile - 1) / p.group_tile;
+    if (table)
+        p.table.assign(table, table + size_t(L.batch) * width);
+    else
+        p.table.clear();
+    p.lengths.assign(lengths, lengths + L.batch);
+
+    // ---------------------------------------------------------------- groups
+    const int T = L.page_size;
+    const int64_t ngroups = int64_t(L.batch) * L.kv_heads * p.group_splits;
+    if (ngroups > INT32_MAX / 2) return fail(PD_ERR_VALUE, "too many (sequence, KV head) groups");
+    std::vector<int64_t> gpages(ngroups);
+    p.groups.assign(size_t(ngroups) * 8, 0);
+    int64_t total = 0;
+    for (int b = 0, gi = 0; b < L.batch; ++b)
+        for (int kvh = 0; kvh < L.kv_heads; ++kvh)
+            for (int gs = 0; gs < p.group_splits; ++gs, ++gi) {
+                int32_t *g = &p.groups[size_t(gi) * 8];
+                g[0] = b;
+                g[1] = kvh;
+                g[2] = kvh * p.group + gs * p.group_tile;
+                g[3] = std::min(p.group_tile, p.group - gs * p.group_tile);
+                g[4] = lengths[b];
+                g[5] = -1;
+                g[6] = 0;
+                gpages[gi] = (int64_t(lengths[b]) + T - 1) / T;
+                total += gpages[gi];
+            }
+    if (total > INT32_MAX) return fail(PD_ERR_VALUE, "too many page tiles per decode step");
+    p.total_pages = total;
+
+    // ---------------------------------------------------------------- balance
+    int64_t C = num_ctas > 0 ? num_ctas : std::max(1, sm_count);
+    C = std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total)));
+    p.num_ctas = int32_t(C);
+    auto bound = [&](int64_t c) { return c * total / C; };   // start of CTA c's range
+    std::vector<std::vector<int32_t>> per(C);
+    std::vector<int32_t> seg_count(ngroups, 0);
+    int64_t cursor = 0, c = 0, empty = 0;
+    for (int64_t gi = 0; gi < ngroups; ++gi) {
+        const int64_t np = gpages[gi];
+        if (np == 0) {
+            // empty sequence: a zero-page segment writes its zero rows
+            auto &v = per[empty++ % C];
+            v.insert(v.end(), {int32_t(gi), 0, 0, -1});
+            seg_count[gi] = 1;
+            continue;
+        }
+        int64_t start = cursor;
+        const int64_t end = cursor + np;
+        while (start < end) {
+            while (bound(c + 1) <= start) ++c;
+            const int64_t stop = std::min(end, bound(c + 1));
+            per[c].insert(per[c].end(), {int32_t(gi), int32_t(start - cursor),
+                                         int32_t(stop - cursor), 0});
+            ++seg_count[gi];
+            start = stop;
+        }
+        cursor = end;
+    }
+    // pieces: a group with more than one segment gets consecutive partial slots
+    std::vector<int32_t> next_piece(ngroups, -1);
+    int32_t pieces = 0;
+    for (int64_t gi = 0; gi < ngroups; ++gi) {
+        int32_t *g = &p.groups[size_t(gi) * 8];
+        if (seg_count[gi] > 1) {
+            g[5] = pieces;
+            g[6] = seg_count[gi];
+            next_piece[gi] = pieces;
+            pieces += seg_count[gi];
+        } else {
+            g[5] = -1;
+            g[6] = 1;
+        }
+    }
+    p.num_pieces = pieces;
+    p.cta_off.assign(size_t(C) + 1, 0);
+    p.segs.clear();
+    for (int64_t i = 0; i < C; ++i) {
+        for (size_t k = 0; k < per[i].size(); k += 4) {
+            int32_t *s = &per[i][k];
+            const int32_t gi = s[0];
+            s[3] = seg_count[gi] > 1 ? next_piece[gi]++ : -1;
+        }
+        p.segs.insert(p.segs.end(), per[i].begin(), per[i].end());
+        p.cta_off[i + 1] = int32_t(p.segs.size() / 4);
+    }
+
+    // ---------------------------------------------------------------- device image
+    DeviceImage &im = p.image;
+    size_t off = 0;
+    im.off_error = off;    off = align256(off + 16);
+    im.off_cta = off;      off = align256(off + p.cta_off.size() * 4);
+    im.off_segs = off;     off = align256(off + p.segs.size() * 4);
+    im.off_groups = off;   off = align256(off + p.groups.size() * 4);
+    im.off_counters = off; off = align256(off + size_t(ngroups) * 4);
+    im.off_table = off;    off = align256(off + p.table.size() * 4);
+    im.off_part_o = off;   off = align256(off + size_t(pieces) * p.group_tile * L.head_dim * 4);
+    im.off_part_ml = off;  off = align256(off + size_t(pieces) * p.group_tile * 8);
+    im.bytes = off;
+    p.host_image.assign(im.off_part_o, 0);
+    std::memcpy(p.host_image.data() + im.off_cta, p.cta_off.data(), p.cta_off.size() * 4);
+    std::memcpy(p.host_image.data() + im.off_segs, p.segs.data(), p.segs.size() * 4);
+    std::memcpy(p.host_image.data() + im.off_groups, p.groups.data(), p.groups.size() * 4);
+    if (!p.table.empty())
+        std::memcpy(p.host_image.data() + im.off_table, p.table.data(), p.table.size() * 4);
+    return PD_OK;
+}
+
+}  // namespace pd

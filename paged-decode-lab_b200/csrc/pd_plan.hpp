@@ -1,0 +1,69 @@
+// pd_plan.hpp — host-side plan: metadata validation, work balancing, device image.
+#pragma once
+
+#include <cuda.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/paged_decode.h"
+
+namespace pd {
+
+// Message of the last failing call on this thread (pd_last_error).
+void set_error(const std::string &msg);
+pd_status fail(pd_status status, const std::string &msg);
+const std::string &last_error();
+
+struct DeviceImage {
+    size_t off_error = 0, off_cta = 0, off_segs = 0, off_groups = 0, off_counters = 0;
+    size_t off_table = 0, off_part_o = 0, off_part_ml = 0, bytes = 0;
+};
+
+struct TensorMapCache {
+    const void *k = nullptr;
+    const void *v = nullptr;
+    int dtype = -1;
+    alignas(64) CUtensorMap map_k;
+    alignas(64) CUtensorMap map_v;
+};
+
+}  // namespace pd
+
+struct pd_plan {
+    pd_layout layout{};
+    int64_t width = 0;             // logical pages per table row
+    int32_t split_tokens = 0;
+    int32_t merge_mode = 0;
+    int32_t device = -1;
+    int32_t group = 0;             // G = Hq / Hkv
+    int32_t group_tile = 8;        // GT: query heads processed together (8, 16, 32)
+    int32_t group_splits = 1;      // ceil(G / GT)
+    int32_t num_ctas = 0;
+    int32_t splits = 1;
+    int32_t max_context = 0;
+    int32_t num_pieces = 0;
+    int64_t total_pages = 0;
+    std::vector<int32_t> table;    // [B * W]
+    std::vector<int32_t> lengths;  // [B]
+    std::vector<int32_t> cta_off;  // [C + 1]
+    std::vector<int32_t> segs;     // 4 per segment
+    std::vector<int32_t> groups;   // 8 per group
+    pd::DeviceImage image;
+    std::vector<uint8_t> host_image;  // metadata part of the device buffer
+    uint8_t *dev = nullptr;           // bound device buffer (caller-owned)
+    size_t dev_bytes = 0;
+    pd::TensorMapCache tmaps;
+};
+
+namespace pd {
+
+// Validate metadata and build the balanced work list; `sm_count` is used when
+// num_ctas <= 0.  Mirrors the checks of runtime.py:33-51 and oracle.py:20-47.
+pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
+                     const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
+                     int32_t num_ctas, int32_t sm_count, pd_plan &plan);
+
+}  // namespace pd

@@ -1,0 +1,243 @@
+"""Validated, allocation-free decode plans over the sm_100a kernel library.
+
+``DecodePlan`` keeps the reference's surface (src/paged_decode/runtime.py:23-90):
+same constructor arguments, the same attributes (``layout``, ``split_tokens``,
+``splits``, ``max_context``, ``merge``, ``merge_implementation``, ``device``,
+``workspace_bytes``), the same exceptions, and ``run`` returning the borrowed
+FP32 [batch, query_heads, head_dim] output.  Underneath, the plan is built by
+the C ABI (include/paged_decode.h): metadata is validated, the pages of all
+(sequence, KV head) groups are balanced across one persistent CTA per SM, and
+metadata plus split-K workspace live in one device buffer that this class
+allocates through PyTorch.  ``run`` allocates nothing and never synchronises,
+so it can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+
+from . import _native
+from .layout import Layout, validate_metadata
+
+__all__ = ["DecodePlan", "inspect_plan", "load_extension"]
+
+
+def load_extension():
+    """Load the prebuilt native library (the reference JIT-compiles here, runtime.py:9-20)."""
+    return _native.load()
+
+
+def _check_limits(layout, split_tokens, merge):
+    if merge not in ("serial", "shared"):
+        raise ValueError("merge must be 'serial' or 'shared'")
+    if layout.head_dim not in (64, 128):
+        raise ValueError("head_dim must be 64 or 128")
+    if layout.page_size not in (16, 32):
+        raise ValueError("page_size must be 16 or 32")
+    if layout.batch > 65535 or layout.query_heads > 65535:
+        raise ValueError("batch/head count exceeds CUDA grid limits")
+    if isinstance(split_tokens, bool) or not isinstance(split_tokens, int) or \
+            not 1 <= split_tokens <= 1048576:
+        raise ValueError("split_tokens must be an integer in [1,1048576]")
+
+
+def _native_plan(layout, table, lengths, split_tokens, merge, device_index, num_ctas):
+    lib = _native.load()
+    c_layout = _native.Layout(layout.batch, layout.query_heads, layout.kv_heads, layout.head_dim,
+                              layout.page_size, layout.physical_pages)
+    table = np.ascontiguousarray(table, dtype=np.int32)
+    lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+    handle = ctypes.c_void_p()
+    _native.check(lib.pd_plan_create(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
+                                     lengths.ctypes.data, split_tokens, int(merge == "shared"),
+                                     device_index, num_ctas or 0, ctypes.byref(handle)),
+                  "plan")
+    return handle
+
+
+def _worklist(lib, handle):
+    info = _native.PlanInfo()
+    _native.check(lib.pd_plan_get_info(handle, ctypes.byref(info)))
+    segs = np.empty((info.num_segments, 4), dtype=np.int32)
+    groups = np.empty((info.num_groups, 8), dtype=np.int32)
+    offsets = np.empty(info.num_ctas + 1, dtype=np.int32)
+    _native.check(lib.pd_plan_copy_worklist(handle, segs.ctypes.data, groups.ctypes.data,
+                                            offsets.ctypes.data))
+    return info, segs, groups, offsets
+
+
+def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=148):
+    """Build a host-only plan (no GPU needed) and return its work list.
+
+    Returns a dict with ``info`` (pd_plan_info fields), ``segments``
+    [n, 4] = (group, first_page, end_page, piece), ``groups`` [g, 8] =
+    (batch, kv_head, first_query_head, query_heads, length, first_piece,
+    pieces, 0) and ``cta_offsets`` [num_ctas + 1].
+    """
+    _check_limits(layout, split_tokens, "serial")
+    table, lengths = validate_metadata(layout, table, lengths)
+    lib = _native.load()
+    handle = _native_plan(layout, table, lengths, split_tokens, "serial", -1, num_ctas)
+    try:
+        info, segs, groups, offsets = _worklist(lib, handle)
+    finally:
+        lib.pd_plan_destroy(handle)
+    return {"info": {name: getattr(info, name) for name, _ in info._fields_},
+            "segments": segs, "groups": groups, "cta_offsets": offsets}
+
+
+class DecodePlan:
+    """Static metadata + reusable workspace for one decode shape.
+
+    table/lengths are CPU integer arrays and are copied during construction.
+    KV contents and q can change between runs; metadata requires a new plan.
+    The output is borrowed storage, overwritten by the next run.  A plan may
+    be used on one stream at a time; use distinct plans for concurrent streams.
+
+    ``merge`` is accepted for compatibility: the B200 kernel always merges
+    split partials inside the decode kernel (the last CTA of a group merges),
+    and ``merge_implementation`` keeps the reference's classification
+    ("serial", "shared" or "serial_fallback", runtime.py:54).
+    ``num_ctas`` (extension) overrides the persistent grid size, which by
+    default is one CTA per SM.
+    """
+
+    def __init__(self, layout: Layout, table, lengths, *, device="cuda", split_tokens=256,
+                 merge="serial", num_ctas=None):
+        import torch
+        _check_limits(layout, split_tokens, merge)
+        table, lengths = validate_metadata(layout, table, lengths)
+        if table.shape[1] > 65536:
+            raise ValueError("page table width must not exceed 65536")
+        self.max_context = int(lengths.max(initial=0))
+        if self.max_context > 1048576:
+            raise ValueError("this implementation supports at most 1M context tokens")
+        self.splits = max(1, math.ceil(self.max_context / split_tokens))
+        if self.splits > 65535:
+            raise ValueError("too many context splits")
+        self.layout, self.split_tokens = layout, split_tokens
+        self.merge = merge
+        self.merge_implementation = (("shared" if self.splits * 4 <= 4096 else "serial_fallback")
+                                     if merge == "shared" else "serial")
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DecodePlan requires a CUDA device")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self._table_cpu, self._lengths_cpu = table, lengths
+        self._lib = _native.load()
+        self._handle = _native_plan(layout, table, lengths, split_tokens, merge,
+                                    self.device.index, num_ctas)
+        self.info, self._segments, self._groups, self._cta_offsets = _worklist(self._lib, self._handle)
+        nbytes = int(self._lib.pd_plan_device_bytes(self._handle))
+        self._buffer = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
+                                dtype=torch.float32, device=self.device)
+        self._bind()
+
+    def _bind(self):
+        import torch
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_plan_bind(self._handle, self._buffer.data_ptr(),
+                                             self._buffer.numel(), stream), "bind")
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle:
+            self._lib.pd_plan_destroy(handle)
+            self._handle = None
+
+    @property
+    def workspace_bytes(self):
+        """Split-K partial outputs, their (m, l) pairs and the merge counters."""
+        return int(self.info.workspace_bytes)
+
+    @property
+    def num_ctas(self):
+        return int(self.info.num_ctas)
+
+    def _check_inputs(self, q, k, v):
+        import torch
+        layout = self.layout
+        expected_q = (layout.batch, layout.query_heads, layout.head_dim)
+        expected_k = (layout.physical_pages, layout.page_size, layout.kv_heads, layout.head_dim)
+        if tuple(q.shape) != expected_q or tuple(k.shape) != expected_k or tuple(v.shape) != expected_k:
+            raise ValueError("input shape does not match plan")
+        if q.dtype not in (torch.float16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+            raise TypeError("q/k/v must share float16 or float32 dtype")
+        for tensor in (q, k, v):
+            if tensor.device != self.device or not tensor.is_contiguous():
+                raise ValueError("inputs must be contiguous on the plan device")
+            if tensor.requires_grad:
+                raise ValueError("inference only: detach tensors requiring gradients")
+        return _native.PD_FLOAT16 if q.dtype == torch.float16 else _native.PD_FLOAT32
+
+    def run(self, q, k, v):
+        """Decode one step; returns the plan's borrowed FP32 [B, Hq, D] output."""
+        import torch
+        dtype = self._check_inputs(q, k, v)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_decode(self._handle, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          dtype, self._out.data_ptr(), stream), "decode")
+        return self._out
+
+    def run_with_stats(self, q, k, v, out, stats):
+        """Decode into caller buffers: out FP32 [B,Hq,D] and stats FP32 [B,Hq,2] = (m, l).
+
+        m is the maximum of score*log2(e)/sqrt(D) and l the softmax
+        denominator relative to it (-inf, 0 for an empty sequence); sequence
+        sharding merges such results across GPUs.
+        """
+        import torch
+        dtype = self._check_inputs(q, k, v)
+        layout = self.layout
+        rows = (layout.batch, layout.query_heads)
+        for t, tail in ((out, (layout.head_dim,)), (stats, (2,))):
+            if tuple(t.shape) != rows + tail or t.dtype != torch.float32 or \
+                    t.device != self.device or not t.is_contiguous():
+                raise ValueError("out/stats must be contiguous FP32 [B,Hq,D] / [B,Hq,2] on the plan device")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_decode_with_stats(
+            self._handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), dtype, out.data_ptr(),
+            stats.data_ptr(), stream), "decode")
+        return out, stats
+
+    def gather(self, k, v):
+        """Debug: the live K/V rows of every (sequence, KV head) through the kernel's TMA path.
+
+        Returns dense [B, Hkv, max_context, D] tensors in the cache dtype; rows
+        past a sequence's length are zero.
+        """
+        import torch
+        layout = self.layout
+        q_stub = torch.empty((layout.batch, layout.query_heads, layout.head_dim), dtype=k.dtype,
+                             device=self.device)
+        dtype = self._check_inputs(q_stub, k, v)
+        shape = (layout.batch, layout.kv_heads, max(self.max_context, 1), layout.head_dim)
+        dense_k = torch.zeros(shape, dtype=k.dtype, device=self.device)
+        dense_v = torch.zeros(shape, dtype=k.dtype, device=self.device)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_gather_debug(self._handle, k.data_ptr(), v.data_ptr(), dtype,
+                                                dense_k.data_ptr(), dense_v.data_ptr(), stream),
+                      "gather")
+        return dense_k, dense_v
+
+    def read_errors(self):
+        """Return and clear the device error word (synchronises the current stream)."""
+        import torch
+        word = ctypes.c_uint32(0)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_plan_read_errors(self._handle, ctypes.byref(word), stream))
+        return int(word.value)
+
+    def worklist(self):
+        """(segments, groups, cta_offsets) as NumPy arrays (see ``inspect_plan``)."""
+        return self._segments.copy(), self._groups.copy(), self._cta_offsets.copy()
+
+    def split_bounds(self, b):
+        """The reference's context partitions of sequence b: range(0, max(len,1), split_tokens)."""
+        length = int(self._lengths_cpu[b])
+        return [(s, min(s + self.split_tokens, length))
+                for s in range(0, max(length, 1), self.split_tokens)]

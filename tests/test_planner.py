@@ -1,0 +1,116 @@
+"""Host planner logic (no GPU): the balanced work list covers every live page once.
+
+The plan's unit is a page tile of one group = (sequence, KV head, query-head
+tile).  Invariants checked here, for many shapes and CTA counts:
+  * every group's segments tile [0, ceil(len/T)) exactly, in order, no overlap;
+  * every CTA streams floor or ceil of total_pages / num_ctas pages;
+  * pieces: a group with one segment has piece -1, otherwise consecutive
+    slots piece0 .. piece0+n-1, each used exactly once;
+  * empty sequences appear as zero-page segments (they write zero rows);
+  * the reference's split partitions (range(0, max(len,1), split)) are reported unchanged.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import paged_oracle
+from paged_decode.layout import Layout
+from paged_decode.runtime import inspect_plan
+from paged_decode import workload
+
+
+def check_worklist(layout, table, lengths, plan):
+    info, segs, groups, offs = plan["info"], plan["segments"], plan["groups"], plan["cta_offsets"]
+    T = layout.page_size
+    G = layout.query_heads // layout.kv_heads
+    gt = info["group_tile"]
+    assert gt == (8 if G <= 8 else 16 if G <= 16 else 32)
+    splits = math.ceil(G / gt)
+    assert info["num_groups"] == layout.batch * layout.kv_heads * splits
+    # groups enumerate (b, kvh, head tile) in order
+    for gi, g in enumerate(groups):
+        b, rest = divmod(gi, layout.kv_heads * splits)
+        kvh, s = divmod(rest, splits)
+        assert tuple(g[:5]) == (b, kvh, kvh * G + s * gt, min(gt, G - s * gt), lengths[b])
+    C = info["num_ctas"]
+    assert offs[0] == 0 and offs[-1] == len(segs) and (np.diff(offs) >= 0).all()
+    total = sum(-(-int(lengths[g[0]]) // T) for g in groups)
+    assert info["total_pages"] == total
+    per_cta = [int((segs[offs[c]:offs[c + 1], 2] - segs[offs[c]:offs[c + 1], 1]).sum()) for c in range(C)]
+    if total:
+        assert min(per_cta) >= total // C and max(per_cta) <= -(-total // C)
+    covered = {gi: [] for gi in range(len(groups))}
+    for c in range(C):
+        for s in segs[offs[c]:offs[c + 1]]:
+            covered[int(s[0])].append((int(s[1]), int(s[2]), int(s[3])))
+    used_pieces = []
+    for gi, ranges in covered.items():
+        pages = -(-int(groups[gi][4]) // T)
+        ranges.sort()
+        assert ranges, f"group {gi} has no segment"
+        if pages == 0:
+            assert ranges == [(0, 0, -1)]
+            continue
+        assert ranges[0][0] == 0 and ranges[-1][1] == pages
+        for (a0, a1, _), (b0, b1, _) in zip(ranges, ranges[1:]):
+            assert a1 == b0 and a0 < a1
+        pieces = [r[2] for r in ranges]
+        if len(ranges) == 1:
+            assert pieces == [-1] and groups[gi][5] == -1 and groups[gi][6] == 1
+        else:
+            assert groups[gi][6] == len(ranges)
+            assert sorted(pieces) == list(range(groups[gi][5], groups[gi][5] + len(ranges)))
+            used_pieces += pieces
+    assert sorted(used_pieces) == list(range(info["num_pieces"]))
+
+
+@pytest.mark.parametrize("ctas", [1, 2, 3, 7, 64, 148, 1000])
+@pytest.mark.parametrize("kv_heads,heads", [(2, 8), (1, 32), (4, 4), (1, 64), (2, 24)])
+def test_worklist_invariants_small(ctas, kv_heads, heads):
+    rng = np.random.default_rng(ctas * 31 + heads)
+    layout = Layout(5, heads, kv_heads, 64, 16, 60)
+    lengths = np.array([0, 1, 17, 160, 191], dtype=np.int32)
+    table = rng.integers(0, 60, size=(5, 12)).astype(np.int32)
+    plan = inspect_plan(layout, table, lengths, split_tokens=33, num_ctas=ctas)
+    check_worklist(layout, table, lengths, plan)
+    assert plan["info"]["splits"] == math.ceil(191 / 33)
+
+
+@pytest.mark.parametrize("name", ["c1", "c2", "c3b", "c5"])
+def test_worklist_invariants_baseline_configs(name):
+    w = workload.CONFIGS[name]()
+    plan = inspect_plan(w.layout, w.table, w.lengths, split_tokens=w.split_tokens, num_ctas=148)
+    check_worklist(w.layout, w.table, w.lengths, plan)
+    info = plan["info"]
+    assert info["num_ctas"] == 148
+    assert info["splits"] == max(1, math.ceil(int(w.lengths.max()) / w.split_tokens))
+
+
+def test_all_empty_batch_writes_zero_rows_only():
+    layout = Layout(2, 4, 4, 64, 16, 1026)
+    table = np.arange(1026, dtype=np.int32).reshape(2, 513)
+    plan = inspect_plan(layout, table, np.array([0, 0], dtype=np.int32), split_tokens=257, num_ctas=148)
+    assert plan["info"]["total_pages"] == 0 and plan["info"]["num_ctas"] == 1
+    check_worklist(layout, table, np.array([0, 0]), plan)
+
+
+def test_split_bounds_match_reference_partitions():
+    for length in (0, 1, 255, 256, 257, 8193):
+        for split in (1, 13, 256, 257):
+            if length // split > 2000:
+                continue
+            expected = [(s, min(s + split, length)) for s in range(0, max(length, 1), split)]
+            assert paged_oracle.split_bounds(length, split) == expected
+
+
+def test_plan_errors_mirror_reference_messages():
+    layout = Layout(1, 4, 2, 64, 16, 4)
+    with pytest.raises(ValueError, match="split_tokens"):
+        inspect_plan(layout, [[0, 1]], [17], split_tokens=0)
+    with pytest.raises(ValueError, match="split_tokens"):
+        inspect_plan(layout, [[0, 1]], [17], split_tokens=True)
+    with pytest.raises(ValueError, match="outside physical cache"):
+        inspect_plan(layout, [[0, 9]], [17])
+    with pytest.raises(TypeError):
+        inspect_plan(layout, [[0.0, 1.0]], [17])

@@ -30,15 +30,20 @@ struct KernelEntry {
     size_t smem;
 };
 
-// Consumer warps per CTA and ring slots: 8 consumers (4 when 32 query heads
-// share a KV head, whose accumulators need 128 registers per thread) and a
-// ~128 KiB ring of page tiles.
+// Consumer warps per CTA and ring slots: up to 8 consumers (4 when 32 query
+// heads share a KV head, whose accumulators need 128 registers per thread)
+// and a ~128 KiB ring of page tiles.  SLOTS is a multiple of NC, so slot s is
+// only ever consumed by warp s % NC: a warp then never waits on a barrier
+// phase more than one ahead of the last one it consumed itself (mbarrier
+// parity waits cannot tell phase u from phase u - 2).
 template <typename Elt, int D, int T, int GT, int MODE>
 KernelEntry make_entry() {
-    constexpr int NC = GT == 32 ? 4 : 8;
     constexpr int TILE = 2 * T * D * int(sizeof(Elt));
     constexpr int SL0 = 131072 / TILE;
-    constexpr int SLOTS = SL0 < 2 ? 2 : (SL0 > 32 ? 32 : SL0);
+    constexpr int SL1 = SL0 < 4 ? 4 : (SL0 > 32 ? 32 : SL0);
+    constexpr int NC0 = GT == 32 ? 4 : 8;
+    constexpr int NC = NC0 < SL1 ? NC0 : SL1;
+    constexpr int SLOTS = SL1 / NC * NC;
     using S = KernelShape<Elt, D, T, GT, NC, SLOTS>;
     return {&paged_decode_kernel<Elt, D, T, GT, NC, SLOTS, MODE>, S::THREADS, S::SMEM};
 }

@@ -72,6 +72,10 @@ struct KernelShape {
     static_assert(ROW_BYTES % 128 == 0, "token rows must be whole 128-byte boxes");
     static_assert(HALF_BYTES % 1024 == 0, "tiles must keep 1024-byte swizzle alignment");
     static_assert(SMEM <= 232448, "shared memory budget exceeded");
+    // Slot s is consumed only by warp s % NC (tiles go round-robin to warps and
+    // slots), which keeps every parity wait within one phase of the last
+    // phase that warp consumed on that slot.
+    static_assert(SLOTS % NC == 0, "ring slots must be a multiple of the consumer warps");
 };
 
 struct SmemFlags {

@@ -1,0 +1,406 @@
+#!/usr/bin/env python3
+"""Decode-attention benchmark: achieved HBM TB/s and µs per decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c3a|c3b|c3c|c4|c5] [--no-cpu-baseline]
+
+One step = one DecodePlan.run over one batch: every live K/V row of every
+sequence is read once per KV head.  Default workload
+(B32 ragged lengths 0..8192 with a shared 64-page prefix, 32:8 heads, D128,
+FP16, page 16, split 256), seeded synthetic data.
+
+N > 1 (torchrun, one rank per GPU, NCCL): KV-head sharding with weak scaling.
+Every rank serves the same sequences (same page tables and lengths) for its
+own 8 KV heads and their 32 query heads, i.e. rank r owns KV heads
+[8r, 8r+8) of an 8N-KV-head model; there is no data-path collective.
+value = all ranks' algorithmic bytes / max-over-ranks step time.
+
+Timing: W untimed warm-up steps, then K steps bracketed by barrier +
+synchronize, device time from CUDA events on the launching stream; each step
+is also timed alone for the kernel's average duration (roofline).  Inputs are
+larger than L2 for config 2; smaller workloads flush L2 between steps.
+e2e: the same step through the public API with host buffers: q copied from
+pinned host memory, decode, FP32 output copied back, every step.
+
+--impl reference: the reference's CPU path (FP64 dense attention, our C port
+of src/paged_decode/oracle.py:59-71, all host threads) on a bounded sample of
+the same workload, plus the reference's own CUDA kernel (built from its
+sources for sm_100a) on the same inputs as an extra field.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "paged-decode-lab_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn µs/step + achieved HBM TB/s vs ~8 TB/s peak at 1/2/4/8 B200"
+L2_BYTES = 126 * 2**20
+DEFAULT_STEPS, DEFAULT_WARMUP = 50, 5
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the decode kernel,
+# from the ncu captures summarised in profiles/ (None until captured).
+NCU_TRAFFIC_BYTES = {}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=DEFAULT_STEPS)
+    ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3a", "c3b", "c3c", "c4", "c5"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------- helpers
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def algorithmic_bytes(w):
+    """Unique live K/V rows of every KV head + q + FP32 out + live table entries."""
+    import numpy as np
+    L = w.layout
+    elt = 2 if w.dtype == "float16" else 4
+    slots = []
+    entries = 0
+    for b in range(L.batch):
+        n = int(w.lengths[b])
+        entries += -(-n // L.page_size)
+        tok = np.arange(n, dtype=np.int64)
+        slots.append(w.table[b][tok // L.page_size].astype(np.int64) * L.page_size + tok % L.page_size)
+    unique = int(np.unique(np.concatenate(slots)).size) if slots else 0
+    return (2 * unique * L.kv_heads * L.head_dim * elt
+            + L.batch * L.query_heads * L.head_dim * (elt + 4) + entries * 4)
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, local, world
+
+
+def max_over_ranks(value, world):
+    import torch
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------- CPU baseline
+def cpu_baseline(w, q, k, v, nbytes, budget_s, steps=None):
+    """FP64 C port of the reference's dense_attention, all host threads, on the workload.
+
+    Runs whole decode steps until ``budget_s`` seconds of CPU time have passed
+    (or ``steps`` times); value = algorithmic bytes per step * steps / seconds.
+    """
+    from oracle import c_oracle
+    threads = os.cpu_count() or 1
+    qh, kh, vh = (t.cpu().numpy() for t in (q, k, v))
+    done, t0 = 0, time.perf_counter()
+    while True:
+        c_oracle.dense_attention(qh, kh, vh, w.table, w.lengths, threads=threads)
+        done += 1
+        elapsed = time.perf_counter() - t0
+        if (steps is not None and done >= steps) or (steps is None and elapsed >= budget_s):
+            break
+    return {"value": nbytes * done / elapsed / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{done} full decode step(s) of {w.name} in {elapsed:.2f} s "
+                      f"(FP64 C restatement of oracle.dense_attention, {threads} threads)",
+            "s_per_step": elapsed / done}
+
+
+# ---------------------------------------------------------------------- our implementation
+def run_ours(args, rank, local, world):
+    import numpy as np
+    import torch
+    from paged_decode import workload
+    from paged_decode.runtime import DecodePlan
+
+    w = workload.CONFIGS[args.workload]()
+    w.seed = w.seed + rank          # rank r: its own KV heads' data, same sequences
+    q, k, v = w.tensors("cuda")
+    plan = DecodePlan(w.layout, w.table, w.lengths, split_tokens=w.split_tokens)
+    nbytes = algorithmic_bytes(w)
+    kv_bytes = 2 * k.numel() * k.element_size()
+    flush = None
+    if kv_bytes < 2 * L2_BYTES:
+        flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return plan.run(q, k, v)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    barrier(world)
+
+    # (1) K back-to-back steps, bracketed; each launch also has its own events
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        t_start.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t_end.record(stream)
+        barrier(world)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = t_start.elapsed_time(t_end)
+    if flush is not None:            # flushes sit between steps: count kernel time only
+        total_ms = sum(launch_ms)
+    step_ms = max_over_ranks(total_ms / args.steps, world)
+    kernel_ms = statistics.mean(launch_ms)
+    errors = plan.read_errors()
+    if errors:
+        raise SystemExit(f"device error word {errors:#x}")
+
+    # (2) e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        q_host = q.cpu().pin_memory()
+        out_host = torch.empty(plan._out.shape, dtype=torch.float32).pin_memory()
+        q_dev = torch.empty_like(q)
+        for _ in range(max(args.warmup, 1)):
+            q_dev.copy_(q_host, non_blocking=True)
+            out_host.copy_(plan.run(q_dev, k, v), non_blocking=True)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_launch = []
+        e0.record(stream)
+        for _ in range(args.steps):
+            if flush is not None:
+                s0 = torch.cuda.Event(enable_timing=True)
+                s1 = torch.cuda.Event(enable_timing=True)
+                flush.zero_()
+                s0.record(stream)
+            q_dev.copy_(q_host, non_blocking=True)
+            out_host.copy_(plan.run(q_dev, k, v), non_blocking=True)
+            if flush is not None:
+                s1.record(stream)
+                e2e_launch.append((s0, s1))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        if flush is not None:
+            e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_launch) / args.steps
+        e2e_ms = max_over_ranks(e2e_ms, world)
+        e2e = {"value": world * nbytes / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
+               "us_per_step": e2e_ms * 1e3,
+               "h2d_bytes_per_step": q.numel() * q.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * 4,
+               "path": "DecodePlan.run (ctypes -> C ABI pd_decode) with pinned host q/out"}
+
+    peak, peak_kind = measured_peak()
+    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+    line = {
+        "metric": METRIC,
+        "value": world * nbytes / (step_ms * 1e-3) / 1e12,
+        "unit": "TB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "us_per_step": step_ms * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16" if w.dtype == "float16" else "f32",
+        "data": "synthetic: seeded N(0,1) tensors, BASELINE config generators (no dataset exists)",
+        "config": {"workload": w.name, "batch": w.layout.batch, "query_heads": w.layout.query_heads,
+                   "kv_heads": w.layout.kv_heads, "head_dim": w.layout.head_dim,
+                   "page_size": w.layout.page_size, "split_tokens": w.split_tokens,
+                   "bytes_per_step_per_gpu": nbytes,
+                   "sharding": ("none" if world == 1 else
+                                f"kv_head, weak: rank r owns KV heads [8r, 8r+8) of a {8 * world}-KV-head "
+                                "model, same sequences on every rank, no collective"),
+                   "l2": ("inputs larger than L2" if flush is None else "L2 flushed between steps"),
+                   "persistent_ctas": plan.num_ctas},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "kernel": "paged_decode_kernel",
+                     "kernel_us": kernel_ms * 1e3,
+                     "algorithmic_bytes_per_launch": nbytes},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, q, k, v, nbytes, args.cpu_seconds)
+    return line
+
+
+# ---------------------------------------------------------------------- reference arm
+def run_reference(args, rank, local, world):
+    import torch
+    from paged_decode import workload
+
+    if rank != 0:
+        return None
+    w = workload.CONFIGS[args.workload]()
+    q, k, v = w.tensors("cuda")
+    nbytes = algorithmic_bytes(w)
+    samples = []
+    t0 = time.perf_counter()
+    for _ in range(max(args.warmup, 0)):
+        cpu_baseline(w, q, k, v, nbytes, 0, steps=1)
+    for _ in range(args.steps):
+        samples.append(cpu_baseline(w, q, k, v, nbytes, 0, steps=1))
+    s_per_step = statistics.mean(s["s_per_step"] for s in samples)
+    value = nbytes / s_per_step / 1e12
+    base = samples[0]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": s_per_step * 1e3,
+        "us_per_step": s_per_step * 1e6, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic: seeded N(0,1) tensors, BASELINE config generators (no dataset exists)",
+        "config": {"workload": w.name, "bytes_per_step_per_gpu": nbytes},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": base["cores"], "kind": "port",
+                         "sample": f"{args.steps} timed full decode steps of {w.name} (FP64 C restatement "
+                                   f"of the reference oracle.dense_attention, {base['cores']} threads)"},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+    # The reference's own CUDA kernel on this B200 (built from its sources), same inputs.
+    try:
+        from oracle import ref_kernel
+        if ref_kernel.SO_PATH.exists():
+            ref = {}
+            for merge in ("serial", "shared"):
+                plan = ref_kernel.RefPlan(w.layout, w.table, w.lengths, device=q.device,
+                                          split_tokens=w.split_tokens, merge=merge)
+                for _ in range(3):
+                    plan.run(q, k, v)
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(10):
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record()
+                    plan.run(q, k, v)
+                    e.record()
+                    e.synchronize()
+                    times.append(s.elapsed_time(e))
+                ms = statistics.median(times)
+                ref[merge] = {"us_per_step": ms * 1e3, "TB/s": nbytes / (ms * 1e-3) / 1e12}
+            line["ref_cuda_b200"] = ref
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal: the CPU arm is the line's value
+        line["ref_cuda_b200"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    return line
+
+
+def main():
+    args = parse_args()
+    if args.steps < 1 or args.warmup < 0:
+        raise SystemExit("--steps >= 1 and --warmup >= 0 required")
+    if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
+        return                      # the reference arm runs on rank 0 only
+    if args.impl == "reference":
+        os.environ["WORLD_SIZE"] = "1"
+        args.gpus = 1
+    rank, local, world = dist_setup(args)
+    try:
+        line = (run_reference if args.impl == "reference" else run_ours)(args, rank, local, world)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -69,9 +69,10 @@ typedef struct pd_plan_info {
     int32_t max_context;     /* max(lengths) */
     int32_t num_ctas;        /* persistent CTAs the decode kernel launches */
     int32_t num_segments;    /* (group, page range) work segments over all CTAs */
-    int32_t num_groups;      /* (sequence, KV head, query-head tile) groups */
+    int32_t num_groups;      /* (sequence, KV-head group, query-head tile) groups */
     int32_t num_pieces;      /* segments of groups that span >1 CTA: partials to merge */
     int32_t group_tile;      /* query heads per group tile (8, 16 or 32) */
+    int32_t heads_per_tile;  /* KV heads gathered per page tile (1, 2, 4 or 8) */
     int32_t total_pages;     /* page tiles streamed per decode (all groups) */
     int64_t workspace_bytes; /* split-K partials + merge counters */
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
@@ -94,8 +95,11 @@ pd_status pd_plan_get_info(const pd_plan *plan, pd_plan_info *info);
 
 /* Work list, for inspection and tests: segments as int32 quadruples
  * (group, first_page, end_page, piece or -1), groups as int32 octuples
- * (batch, kv_head, first_query_head, query_heads, length, first_piece, pieces, 0)
- * and per-CTA segment offsets [num_ctas + 1].  Any pointer may be NULL.
+ * (batch, first_kv_head, query_head_offset, query_heads, length, first_piece,
+ * pieces, 0): the group covers heads_per_tile KV heads from first_kv_head and,
+ * of each one's G query heads, query_heads of them from query_head_offset;
+ * cta_offsets receives the per-CTA segment offsets [num_ctas + 1].  Any
+ * pointer may be NULL.
  */
 pd_status pd_plan_copy_worklist(const pd_plan *plan, int32_t *segments, int32_t *groups,
                                 int32_t *cta_offsets);

@@ -12,7 +12,7 @@
 #include <type_traits>
 #include <utility>
 
-#include "pd_decode_kernel.cuh"
+#include "pd_kernels.cuh"
 #include "pd_plan.hpp"
 
 #define PD_API extern "C" __attribute__((visibility("default")))
@@ -22,51 +22,13 @@ const std::string &last_error();
 
 namespace {
 
-using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const DecodeArgs);
-
-struct KernelEntry {
-    KernelFn fn;
-    int threads;
-    size_t smem;
-};
-
-// Consumer warps per CTA and ring slots: up to 8 consumers (4 when 32 query
-// heads share a KV head, whose accumulators need 128 registers per thread)
-// and a ~128 KiB ring of page tiles.  SLOTS is a multiple of NC, so slot s is
-// only ever consumed by warp s % NC: a warp then never waits on a barrier
-// phase more than one ahead of the last one it consumed itself (mbarrier
-// parity waits cannot tell phase u from phase u - 2).
-template <typename Elt, int D, int T, int GT, int MODE>
-KernelEntry make_entry() {
-    constexpr int TILE = 2 * T * D * int(sizeof(Elt));
-    constexpr int SL0 = 131072 / TILE;
-    constexpr int SL1 = SL0 < 4 ? 4 : (SL0 > 32 ? 32 : SL0);
-    constexpr int NC0 = GT == 32 ? 4 : 8;
-    constexpr int NC = NC0 < SL1 ? NC0 : SL1;
-    constexpr int SLOTS = SL1 / NC * NC;
-    using S = KernelShape<Elt, D, T, GT, NC, SLOTS>;
-    return {&paged_decode_kernel<Elt, D, T, GT, NC, SLOTS, MODE>, S::THREADS, S::SMEM};
-}
-
-template <typename Elt, int D, int T, int MODE>
-KernelEntry entry_gt(int gt) {
-    if (MODE == kModeGather || gt == 8) return make_entry<Elt, D, T, 8, MODE>();
-    if (gt == 16) return make_entry<Elt, D, T, 16, MODE>();
-    return make_entry<Elt, D, T, 32, MODE>();
-}
-
-template <typename Elt, int MODE>
-KernelEntry entry_dt(int D, int T, int gt) {
-    if (D == 64) return T == 16 ? entry_gt<Elt, 64, 16, MODE>(gt) : entry_gt<Elt, 64, 32, MODE>(gt);
-    return T == 16 ? entry_gt<Elt, 128, 16, MODE>(gt) : entry_gt<Elt, 128, 32, MODE>(gt);
-}
-
-KernelEntry kernel_for(pd_dtype dtype, int D, int T, int gt, int mode) {
-    if (dtype == PD_FLOAT16)
-        return mode == kModeDecode ? entry_dt<__half, kModeDecode>(D, T, gt)
-                                   : entry_dt<__half, kModeGather>(D, T, gt);
-    return mode == kModeDecode ? entry_dt<float, kModeDecode>(D, T, gt)
-                               : entry_dt<float, kModeGather>(D, T, gt);
+KernelEntry kernel_for(pd_dtype dtype, int D, int T, int gt, int hg, int mode) {
+    if (dtype == PD_FLOAT16) {
+        if (D == 64) return T == 16 ? kernel_entry_f16_d64_t16(gt, hg, mode) : kernel_entry_f16_d64_t32(gt, hg, mode);
+        return T == 16 ? kernel_entry_f16_d128_t16(gt, hg, mode) : kernel_entry_f16_d128_t32(gt, hg, mode);
+    }
+    if (D == 64) return T == 16 ? kernel_entry_f32_d64_t16(gt, hg, mode) : kernel_entry_f32_d64_t32(gt, hg, mode);
+    return T == 16 ? kernel_entry_f32_d128_t16(gt, hg, mode) : kernel_entry_f32_d128_t32(gt, hg, mode);
 }
 
 std::mutex g_attr_mutex;
@@ -98,22 +60,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// K or V cache [P, T, Hkv, D] viewed as 3-D {D, Hkv, P*T}: one box = the T
-// token rows of one page for one KV head, 128 bytes of head dims wide.
-pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, CUtensorMap *map) {
+// K or V cache [P, T, Hkv, D] viewed as 4-D {D, T, Hkv, P} (strides in bytes:
+// elt, Hkv*D*elt, D*elt, T*Hkv*D*elt).  One box = 128 bytes of head dims x
+// all T tokens x HG KV heads of one page, landing in shared memory as
+// [head][token] rows of 128 bytes, so the 128-byte swizzle XORs by token.
+pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, int hg, CUtensorMap *map) {
     auto encode = tensor_map_encoder();
     if (!encode) return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    const int elt = dtype == PD_FLOAT16 ? 2 : 4;
+    const cuuint64_t elt = dtype == PD_FLOAT16 ? 2 : 4;
     const pd_layout &L = p.layout;
-    cuuint64_t dims[3] = {cuuint64_t(L.head_dim), cuuint64_t(L.kv_heads),
-                          cuuint64_t(L.physical_pages) * cuuint64_t(L.page_size)};
-    cuuint64_t strides[2] = {cuuint64_t(L.head_dim) * elt, cuuint64_t(L.kv_heads) * L.head_dim * elt};
-    cuuint32_t box[3] = {cuuint32_t(128 / elt), 1, cuuint32_t(L.page_size)};
-    cuuint32_t estr[3] = {1, 1, 1};
+    const cuuint64_t row = cuuint64_t(L.head_dim) * elt;
+    cuuint64_t dims[4] = {cuuint64_t(L.head_dim), cuuint64_t(L.page_size), cuuint64_t(L.kv_heads),
+                          cuuint64_t(L.physical_pages)};
+    cuuint64_t strides[3] = {row * cuuint64_t(L.kv_heads), row, row * cuuint64_t(L.kv_heads) * L.page_size};
+    cuuint32_t box[4] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(hg), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = encode(map,
                               dtype == PD_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                              3, const_cast<void *>(base), dims, strides, box, estr,
+                              4, const_cast<void *>(base), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
@@ -165,6 +130,7 @@ DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
     a.Hkv = p->layout.kv_heads;
     a.W = int32_t(p->width);
     a.max_len = p->max_context;
+    a.group = p->group;
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
@@ -177,15 +143,16 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
         return fail(PD_ERR_VALUE, "k and v must be 16-byte aligned");
     TensorMapCache &tc = p->tmaps;
     if (tc.k != k || tc.v != v || tc.dtype != int(dtype)) {
-        pd_status s = encode_cache_map(*p, k, dtype, &tc.map_k);
+        pd_status s = encode_cache_map(*p, k, dtype, p->heads_per_tile, &tc.map_k);
         if (s != PD_OK) return s;
-        s = encode_cache_map(*p, v, dtype, &tc.map_v);
+        s = encode_cache_map(*p, v, dtype, p->heads_per_tile, &tc.map_v);
         if (s != PD_OK) return s;
         tc.k = k;
         tc.v = v;
         tc.dtype = int(dtype);
     }
-    const KernelEntry e = kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, mode);
+    const KernelEntry e =
+        kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode);
     pd_status s = ensure_smem_attribute(p->device, e);
     if (s != PD_OK) return s;
     e.fn<<<p->num_ctas, e.threads, e.smem, static_cast<cudaStream_t>(stream)>>>(tc.map_k, tc.map_v,
@@ -253,6 +220,7 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->num_groups = int32_t(p->groups.size() / 8);
     info->num_pieces = p->num_pieces;
     info->group_tile = p->group_tile;
+    info->heads_per_tile = p->heads_per_tile;
     info->total_pages = int32_t(p->total_pages);
     info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o) +
                             int64_t(p->groups.size() / 8) * 4;
@@ -309,12 +277,9 @@ PD_API pd_status pd_merge_shards(const float *shard_out, const float *shard_stat
     if (shards < 1 || rows < 0 || head_dim <= 0)
         return fail(PD_ERR_VALUE, "shards >= 1, rows >= 0 and head_dim > 0 required");
     if (rows == 0) return PD_OK;
-    constexpr int kRowsPerBlock = 8;
-    const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-    if (blocks > INT32_MAX) return fail(PD_ERR_VALUE, "too many rows");
-    merge_shards_kernel<<<unsigned(blocks), kRowsPerBlock * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        shard_out, reinterpret_cast<const float2 *>(shard_stats), shards, rows, head_dim, out);
-    const cudaError_t err = cudaGetLastError();
+    if ((rows + 7) / 8 > INT32_MAX) return fail(PD_ERR_VALUE, "too many rows");
+    const cudaError_t err =
+        launch_merge_shards(shard_out, shard_stats, shards, rows, head_dim, out, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
     return PD_OK;

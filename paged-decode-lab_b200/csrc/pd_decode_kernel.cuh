@@ -4,21 +4,26 @@
 // (src/paged_decode/csrc/decode.cu:26-168) with one persistent kernel:
 //
 //   * one CTA per SM walks a host-built list of segments; a segment is a run
-//     of logical pages of one group = (sequence, KV head, query-head tile);
-//     the host balances pages across CTAs, so every SM streams the same bytes;
-//   * warp NC (producer) looks up each page in the page table and gathers its
-//     K and V rows for the segment's KV head with 3-D tiled TMA loads
-//     (128-byte swizzle, no multicast) into a ring of shared-memory slots,
-//     completion tracked by mbarriers;
-//   * warps 0..NC-1 (consumers) take the ring's tiles round-robin and fold
-//     them into a per-warp online softmax (running max m, denominator l,
-//     unnormalised output o) for all G query heads of the KV head at once:
-//     FP16 inputs use m16n8k16 tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T,
-//     FP32 accumulators), FP32 inputs use FP32 FMAs;
-//   * at a segment's end the consumer warps combine their states through
-//     shared memory; a group owned by one CTA writes its normalised output
-//     directly, otherwise each CTA writes an (m, l, o) partial and the CTA
-//     that arrives last (atomic counter, reset after use) merges them.
+//     of logical pages of one group = (sequence, KV-head group of HG heads,
+//     query-head tile); the host balances page tiles across CTAs, so every SM
+//     streams the same number of bytes, ragged batches included;
+//   * warp NC (producer) looks up each page in the page table and gathers the
+//     page's K and V rows for all HG KV heads of the group with 4-D tiled TMA
+//     loads ({D, T, Hkv, P} view, 128-byte swizzle, no multicast) into a ring
+//     of shared-memory slots, completion tracked by mbarriers.  Boxes cover
+//     HG heads at once because a TMA instruction costs the same ~75 issue
+//     cycles whatever its size; many bytes per instruction keep one thread
+//     ahead of HBM;
+//   * consumer warp w owns KV head w % HG of the group and takes every
+//     NSUB-th tile (NSUB = NC / HG); it folds its tiles into an online
+//     softmax (running max m, denominator l, unnormalised output o) for all
+//     query heads of that KV head at once: FP16 inputs use m16n8k16
+//     tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T, FP32 accumulators), FP32
+//     inputs use FP32 FMAs;
+//   * at a segment's end the NSUB warps of each KV head combine their states
+//     through shared memory; a group owned by one CTA writes its normalised
+//     output directly, otherwise each CTA writes an (m, l, o) partial and the
+//     CTA that arrives last (atomic counter, reset after use) merges them.
 //
 // All exponentials are base 2 on scores pre-multiplied by log2(e)/sqrt(D);
 // this is the reference's exp(s - m) rewritten, not a different softmax.
@@ -35,16 +40,16 @@ struct DecodeArgs {
     const int32_t *table;     // [B, W]
     const int32_t *cta_off;   // [C + 1] segment range of each CTA
     const int4 *segs;         // {group, first_page, end_page, piece (-1: sole piece)}
-    const int4 *groups;       // 2 per group: {b, kvh, h0, nh}, {length, piece0, npieces, 0}
+    const int4 *groups;       // 2 per group: {b, kv_head0, q_head_offset, nh}, {length, piece0, npieces, 0}
     int32_t *counters;        // [groups] arrivals of multi-piece groups (self-resetting)
-    float *part_o;            // [pieces, GT, D] unnormalised partial outputs
-    float2 *part_ml;          // [pieces, GT] (m, l) of each partial
+    float *part_o;            // [pieces, HG, GT, D] unnormalised partial outputs
+    float2 *part_ml;          // [pieces, HG, GT] (m, l) of each partial
     float *out;               // [B, Hq, D]
     float *stats;             // [B, Hq, 2] (m, l) or nullptr
     uint32_t *error;          // error word (PD_DEVERR_* bits)
     void *dense_k;            // gather mode: [B, Hkv, max_len, D]
     void *dense_v;
-    int32_t Hq, Hkv, W, max_len;
+    int32_t Hq, Hkv, W, max_len, group;   // group = G = Hq / Hkv
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
 };
@@ -52,30 +57,28 @@ struct DecodeArgs {
 constexpr uint32_t kErrTimeout = 1u;
 constexpr uint32_t kErrBadPage = 2u;
 
-template <typename Elt, int D, int T, int GT, int NC, int SLOTS>
+template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS>
 struct KernelShape {
     static constexpr int ELT = sizeof(Elt);
+    static constexpr int NC = HG * NSUB;               // consumer warps
     static constexpr int ROW_BYTES = D * ELT;
     static constexpr int NBOX = ROW_BYTES / 128;       // 128-byte TMA boxes per token row
     static constexpr int BOX_ELEMS = 128 / ELT;
-    static constexpr int HALF_BYTES = T * ROW_BYTES;   // K (or V) part of one page tile
+    static constexpr int ROWS = HG * T;                // swizzle rows per box: [head][token]
+    static constexpr int HALF_BYTES = NBOX * ROWS * 128;  // K (or V) part of one page tile
     static constexpr int TILE_BYTES = 2 * HALF_BYTES;
     static constexpr int OSTRIDE = D + 4;              // padded merge rows: conflict-free stores
     static constexpr int THREADS = (NC + 1) * 32;
     static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
-    static constexpr size_t MERGE_O = size_t(NC) * GT * OSTRIDE * 4;
+    static constexpr size_t MERGE_O = NSUB > 1 ? size_t(NC) * GT * OSTRIDE * 4 : 0;
     static constexpr size_t MERGE_ML = size_t(NC) * GT * 2 * 4;
-    static constexpr size_t QS = size_t(GT) * D * ELT;
+    // FP16 with up to 16 query heads per KV head keeps Q in registers;
+    // otherwise Q of all HG heads is staged in shared memory per segment.
+    static constexpr bool Q_SMEM = !(ELT == 2 && GT <= 16);
+    static constexpr size_t QS = Q_SMEM ? size_t(HG) * GT * D * ELT : 0;
     static constexpr size_t BARS = size_t(SLOTS) * 16;
     static constexpr size_t FLAGS = size_t(SLOTS) * 4 + 16;
     static constexpr size_t SMEM = 1024 + RING + MERGE_O + MERGE_ML + QS + BARS + FLAGS;
-    static_assert(ROW_BYTES % 128 == 0, "token rows must be whole 128-byte boxes");
-    static_assert(HALF_BYTES % 1024 == 0, "tiles must keep 1024-byte swizzle alignment");
-    static_assert(SMEM <= 232448, "shared memory budget exceeded");
-    // Slot s is consumed only by warp s % NC (tiles go round-robin to warps and
-    // slots), which keeps every parity wait within one phase of the last
-    // phase that warp consumed on that slot.
-    static_assert(SLOTS % NC == 0, "ring slots must be a multiple of the consumer warps");
 };
 
 struct SmemFlags {
@@ -85,16 +88,18 @@ struct SmemFlags {
 };
 
 // ------------------------------------------------------------------ FP16 tensor-core engine
-// One warp's online-softmax state for all GT query heads of a KV head.
+// One warp's online-softmax state for the GT query heads of one KV head.
 // S^T[t][g] = K[t][:] . Q[g][:]  with A = K tile (ldmatrix), B = Q^T fragments;
 // O^T[d][g] += V^T[d][t] P^T[t][g] with A = V tile (ldmatrix.trans), B = P^T,
 // where P^T comes from the S^T accumulators by movmatrix.trans (no shared memory).
-template <int D, int T, int GT>
+// Tile rows are [head][token] 128-byte rows; this warp's head starts at row r0.
+template <int D, int T, int GT, int ROWS>
 struct HalfEngine {
     static constexpr int NT = GT / 8;    // n-tiles of 8 query heads
     static constexpr int KS = D / 16;    // k-steps of the QK^T product
     static constexpr int DT = D / 16;    // m-tiles of the PV product (head dims)
     static constexpr int MT = T / 16;    // 16-token m-tiles per page
+    static constexpr int HALF = (D * 2 / 128) * ROWS * 128;
     static constexpr bool Q_REGS = NT <= 2;
 
     uint32_t qf[Q_REGS ? KS : 1][Q_REGS ? NT : 1][2];
@@ -157,8 +162,8 @@ struct HalfEngine {
         }
     }
 
-    __device__ __forceinline__ void tile(uint32_t kbase, int valid, float scale_log2) {
-        const uint32_t vbase = kbase + T * D * 2;
+    __device__ __forceinline__ void tile(uint32_t kbase, int r0, int valid, float scale_log2) {
+        const uint32_t vbase = kbase + HALF;
         const int mi = lane >> 3, r8 = lane & 7;
         float x[MT][NT][4];
 #pragma unroll
@@ -167,11 +172,11 @@ struct HalfEngine {
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) x[mt][nt][i] = 0.f;
-            const int row = mt * 16 + r8 + (mi & 1) * 8;
+            const int row = r0 + mt * 16 + r8 + (mi & 1) * 8;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 uint32_t a[4];
-                ldmatrix_x4(a, kbase + swz128<T>(row, ks * 2 + (mi >> 1)));
+                ldmatrix_x4(a, kbase + swz128<ROWS>(row, ks * 2 + (mi >> 1)));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     uint32_t b0, b1;
@@ -236,19 +241,19 @@ struct HalfEngine {
         }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-            const int row = mt * 16 + r8 + (mi >> 1) * 8;
+            const int row = r0 + mt * 16 + r8 + (mi >> 1) * 8;
 #pragma unroll
             for (int dt = 0; dt < DT; ++dt) {
                 uint32_t a[4];
-                ldmatrix_x4_trans(a, vbase + swz128<T>(row, dt * 2 + (mi & 1)));
+                ldmatrix_x4_trans(a, vbase + swz128<ROWS>(row, dt * 2 + (mi & 1)));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_16816(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
             }
         }
     }
 
-    // Publish (m, l, o) of this warp to the merge buffers.
-    __device__ __forceinline__ void store(float *sm_m, float *sm_l, float *sm_o) {
+    // Reduce l over the lanes sharing a query head; publish m and l (lanes 0-3).
+    __device__ __forceinline__ void finish(float *sm_m, float *sm_l) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -260,22 +265,25 @@ struct HalfEngine {
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
-                    const int g = nt * 8 + 2 * lane + i;
-                    sm_m[g] = m[nt][i];
-                    sm_l[g] = l[nt][i];
+                    sm_m[nt * 8 + 2 * lane + i] = m[nt][i];
+                    sm_l[nt * 8 + 2 * lane + i] = l[nt][i];
                 }
         }
-        constexpr int OS = D + 4;
+    }
+
+    // Call f(g, d, value) for every accumulator element this lane holds.
+    template <typename F>
+    __device__ __forceinline__ void for_each_o(F &&f) const {
 #pragma unroll
         for (int dt = 0; dt < DT; ++dt)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int g = nt * 8 + 2 * (lane & 3);
                 const int d = dt * 16 + (lane >> 2);
-                sm_o[g * OS + d] = acc[dt][nt][0];
-                sm_o[(g + 1) * OS + d] = acc[dt][nt][1];
-                sm_o[g * OS + d + 8] = acc[dt][nt][2];
-                sm_o[(g + 1) * OS + d + 8] = acc[dt][nt][3];
+                f(g, d, acc[dt][nt][0]);
+                f(g + 1, d, acc[dt][nt][1]);
+                f(g, d + 8, acc[dt][nt][2]);
+                f(g + 1, d + 8, acc[dt][nt][3]);
             }
     }
 };
@@ -283,11 +291,12 @@ struct HalfEngine {
 // ------------------------------------------------------------------ FP32 engine
 // Lanes own tokens for the scores (one row of K per lane, Q broadcast from
 // shared memory) and own head dims for the value sum.
-template <int D, int T, int GT>
+template <int D, int T, int GT, int ROWS>
 struct FloatEngine {
-    static constexpr int DPL = D / 32;           // value dims per lane
-    static constexpr int HALVES = 32 / T;        // lanes per token in the score phase
+    static constexpr int DPL = D / 32;             // value dims per lane
+    static constexpr int HALVES = 32 / T;          // lanes per token in the score phase
     static constexpr int CHUNKS = D / 4 / HALVES;  // float4 chunks of K per lane
+    static constexpr int HALF = (D * 4 / 128) * ROWS * 128;
 
     float acc[GT][DPL];
     float m[GT], l[GT];
@@ -307,8 +316,8 @@ struct FloatEngine {
         }
     }
 
-    __device__ __forceinline__ void tile(uint32_t kbase, int valid, float scale_log2) {
-        const uint32_t vbase = kbase + T * D * 4;
+    __device__ __forceinline__ void tile(uint32_t kbase, int r0, int valid, float scale_log2) {
+        const uint32_t vbase = kbase + HALF;
         const int t = lane % T;
         const int half = lane / T;
         float x[GT];
@@ -317,7 +326,7 @@ struct FloatEngine {
 #pragma unroll 4
         for (int c = 0; c < CHUNKS; ++c) {
             const int chunk = half * CHUNKS + c;
-            const float4 kv = lds_f4(kbase + swz128<T>(t, chunk));
+            const float4 kv = lds_f4(kbase + swz128<ROWS>(r0 + t, chunk));
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
                 if (g < nh) {
@@ -353,11 +362,11 @@ struct FloatEngine {
         for (int tt = 0; tt < T; ++tt) {
             float vv[DPL];
             if constexpr (DPL == 2) {
-                const float2 v2 = lds_f2(vbase + swz128<T>(tt, lane >> 1) + (lane & 1) * 8);
+                const float2 v2 = lds_f2(vbase + swz128<ROWS>(r0 + tt, lane >> 1) + (lane & 1) * 8);
                 vv[0] = v2.x;
                 vv[1] = v2.y;
             } else {
-                const float4 v4 = lds_f4(vbase + swz128<T>(tt, lane));
+                const float4 v4 = lds_f4(vbase + swz128<ROWS>(r0 + tt, lane));
                 vv[0] = v4.x;
                 vv[1] = v4.y;
                 vv[2] = v4.z;
@@ -374,48 +383,63 @@ struct FloatEngine {
         }
     }
 
-    __device__ __forceinline__ void store(float *sm_m, float *sm_l, float *sm_o) {
-        constexpr int OS = D + 4;
+    __device__ __forceinline__ void finish(float *sm_m, float *sm_l) {
 #pragma unroll
         for (int g = 0; g < GT; ++g) {
             float s = l[g];
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) s += __shfl_xor_sync(kFullMask, s, o);
+            l[g] = s;
             if (lane == 0) {
                 sm_m[g] = m[g];
                 sm_l[g] = s;
             }
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) sm_o[g * OS + lane * DPL + i] = acc[g][i];
         }
+    }
+
+    template <typename F>
+    __device__ __forceinline__ void for_each_o(F &&f) const {
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) f(g, lane * DPL + i, acc[g][i]);
     }
 };
 
-template <typename Elt, int D, int T, int GT>
+template <typename Elt, int D, int T, int GT, int ROWS>
 struct EngineFor;
-template <int D, int T, int GT>
-struct EngineFor<__half, D, T, GT> {
-    using type = HalfEngine<D, T, GT>;
+template <int D, int T, int GT, int ROWS>
+struct EngineFor<__half, D, T, GT, ROWS> {
+    using type = HalfEngine<D, T, GT, ROWS>;
 };
-template <int D, int T, int GT>
-struct EngineFor<float, D, T, GT> {
-    using type = FloatEngine<D, T, GT>;
+template <int D, int T, int GT, int ROWS>
+struct EngineFor<float, D, T, GT, ROWS> {
+    using type = FloatEngine<D, T, GT, ROWS>;
 };
 
 // ------------------------------------------------------------------ kernel
 enum : int { kModeDecode = 0, kModeGather = 1 };
 
-template <typename Elt, int D, int T, int GT, int NC, int SLOTS, int MODE>
-__global__ void __launch_bounds__((NC + 1) * 32, 1)
+template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS, int MODE>
+__global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
-    using S = KernelShape<Elt, D, T, GT, NC, SLOTS>;
+    using S = KernelShape<Elt, D, T, GT, HG, NSUB, SLOTS>;
+    constexpr int NC = S::NC;
+    static_assert(S::ROW_BYTES % 128 == 0, "token rows must be whole 128-byte boxes");
+    static_assert((S::ROWS * 128) % 1024 == 0, "boxes must keep 1024-byte swizzle alignment");
+    static_assert(S::SMEM <= 232448, "shared memory budget exceeded");
+    // Tile j goes to slot j % SLOTS and to the warps of sub-pipeline j % NSUB;
+    // with SLOTS a multiple of NSUB every slot is consumed by one fixed set of
+    // warps, which keeps every mbarrier parity wait within one phase of the
+    // last phase those warps consumed (parity cannot tell phase u from u - 2).
+    static_assert(SLOTS % NSUB == 0, "ring slots must be a multiple of the sub-pipelines");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
     float *merge_o = reinterpret_cast<float *>(ring + S::RING);
-    float *merge_m = merge_o + size_t(NC) * GT * S::OSTRIDE;
+    float *merge_m = merge_o + S::MERGE_O / 4;
     float *merge_l = merge_m + size_t(NC) * GT;
     uint8_t *qsm = reinterpret_cast<uint8_t *>(merge_l + size_t(NC) * GT);
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(qsm + S::QS);
@@ -431,7 +455,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < SLOTS; ++s) {
             mbar_init(smem_u32(full_bar + s), 1);
-            mbar_init(smem_u32(empty_bar + s), 1);
+            mbar_init(smem_u32(empty_bar + s), HG);   // released by the HG warps that read it
         }
         flags->abort = 0;
         flags->last = 0;
@@ -451,7 +475,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int4 sg = a.segs[si];
             const int4 g0 = a.groups[2 * sg.x];
             const int32_t *trow = a.table + int64_t(g0.x) * a.W;
-            const int kvh = g0.y;
+            const int kv0 = g0.y;
             for (int pg = sg.y; pg < sg.z; pg += 32) {
                 const int n = min(32, sg.z - pg);
                 const int mine = lane < n ? __ldg(trow + pg + lane) : 0;
@@ -472,11 +496,11 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                             const uint32_t dst = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
 #pragma unroll
                             for (int bx = 0; bx < S::NBOX; ++bx)
-                                tma_load_3d(dst + bx * T * 128, &tm_k, bx * S::BOX_ELEMS, kvh, page * T, fb);
+                                tma_load_4d(dst + bx * S::ROWS * 128, &tm_k, bx * S::BOX_ELEMS, 0, kv0, page, fb);
 #pragma unroll
                             for (int bx = 0; bx < S::NBOX; ++bx)
-                                tma_load_3d(dst + S::HALF_BYTES + bx * T * 128, &tm_v, bx * S::BOX_ELEMS,
-                                            kvh, page * T, fb);
+                                tma_load_4d(dst + S::HALF_BYTES + bx * S::ROWS * 128, &tm_v, bx * S::BOX_ELEMS,
+                                            0, kv0, page, fb);
                         } else {
                             // The reference skips tokens whose page id is out of range
                             // (decode.cu:58); plans validate ids, so this is defence only.
@@ -494,20 +518,23 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     // ---------------------------------------------------------------- consumers
     constexpr int CT = NC * 32;
     const int ctid = threadIdx.x;
+    const int hh = warp % HG;       // KV head of the group this warp owns
+    const int sub = warp / HG;      // this warp takes tiles j with j % NSUB == sub
+    const int r0 = hh * T;          // its rows in a [head][token] tile
     bool stop = false;
     int j = 0;
     for (int si = seg_begin; si < seg_end; ++si) {
         const int4 sg = a.segs[si];
         const int4 g0 = a.groups[2 * sg.x];
         const int4 g1 = a.groups[2 * sg.x + 1];
-        const int b = g0.x, kvh = g0.y, h0 = g0.z, nh = g0.w;
+        const int b = g0.x, kv0 = g0.y, qoff = g0.z, nh = g0.w;
         const int length = g1.x;
         const int npg = sg.z - sg.y;
-        const int first = ((warp - j) % NC + NC) % NC;
+        const int first = ((sub - j) % NSUB + NSUB) % NSUB;
 
         if constexpr (MODE == kModeGather) {
             constexpr int CPR = S::ROW_BYTES / 16;   // 16-byte chunks per token row
-            for (int t = first; t < npg; t += NC) {
+            for (int t = first; t < npg; t += NSUB) {
                 const int jj = j + t;
                 const int slot = jj % SLOTS;
                 if (!stop && !flags->abort) {
@@ -520,11 +547,11 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         const int valid = min(T, length - lp * T);
                         if (slot_valid[slot]) {
                             const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
-                            const int64_t base = (int64_t(b) * a.Hkv + kvh) * a.max_len + int64_t(lp) * T;
+                            const int64_t base = (int64_t(b) * a.Hkv + kv0 + hh) * a.max_len + int64_t(lp) * T;
                             for (int idx = lane; idx < valid * CPR; idx += 32) {
                                 const int r = idx / CPR, c = idx % CPR;
-                                const float4 kv = lds_f4(kb + swz128<T>(r, c));
-                                const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<T>(r, c));
+                                const float4 kv = lds_f4(kb + swz128<S::ROWS>(r0 + r, c));
+                                const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<S::ROWS>(r0 + r, c));
                                 const int64_t off = (base + r) * S::ROW_BYTES + c * 16;
                                 *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_k) + off) = kv;
                                 *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_v) + off) = vv;
@@ -538,27 +565,30 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             j += npg;
             continue;
         } else {
-            using Engine = typename EngineFor<Elt, D, T, GT>::type;
+            using Engine = typename EngineFor<Elt, D, T, GT, S::ROWS>::type;
             Engine eng;
-            const Elt *qrow = static_cast<const Elt *>(a.q) + (int64_t(b) * a.Hq + h0) * D;
-            const uint32_t qs = smem_u32(qsm);
-            constexpr bool kQsmem = !std::is_same<Elt, __half>::value || !HalfEngine<D, T, GT>::Q_REGS;
-            if constexpr (kQsmem) {
-                // cooperative Q tile load (zero rows for heads past nh)
-                if constexpr (std::is_same<Elt, float>::value) {
-                    float *qf = reinterpret_cast<float *>(qsm);
-                    for (int e = ctid; e < GT * D; e += CT) {
-                        const int g = e / D;
-                        qf[e] = g < nh ? qrow[e] : 0.f;
-                    }
-                } else {
-                    for (int e = ctid; e < GT * (D / 8); e += CT) {
-                        const int g = e / (D / 8), c = e % (D / 8);
-                        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (g < nh) v = *reinterpret_cast<const float4 *>(qrow + g * D + c * 8);
-                        const int sc = (c & 8) | ((c & 7) ^ (g & 7));
-                        *reinterpret_cast<float4 *>(qsm + g * D * 2 + sc * 16) = v;
-                    }
+            // query heads of this warp's KV head: (kv0 + hh) * G + qoff + g, g < nh
+            const int64_t qhead0 = int64_t(b) * a.Hq + int64_t(kv0 + hh) * a.group + qoff;
+            const Elt *qrow = static_cast<const Elt *>(a.q) + qhead0 * D;
+            uint8_t *qmine = qsm + size_t(hh) * GT * D * sizeof(Elt);
+            const uint32_t qs = smem_u32(qmine);
+            static_assert(!std::is_same<Elt, __half>::value ||
+                              S::Q_SMEM == !HalfEngine<D, T, GT, S::ROWS>::Q_REGS,
+                          "Q staging must match the FP16 engine");
+            if constexpr (S::Q_SMEM) {
+                // cooperative Q load for all HG heads (zero rows for heads past nh)
+                for (int e = ctid; e < HG * GT * (D * int(sizeof(Elt)) / 16); e += CT) {
+                    const int per_head = GT * (D * int(sizeof(Elt)) / 16);
+                    const int h = e / per_head, r = e % per_head;
+                    const int g = r / (D * int(sizeof(Elt)) / 16), c = r % (D * int(sizeof(Elt)) / 16);
+                    const Elt *src = static_cast<const Elt *>(a.q) +
+                                     (int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g) * D;
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (g < nh) v = reinterpret_cast<const float4 *>(src)[c];
+                    uint8_t *dst = qsm + size_t(h) * GT * D * sizeof(Elt) + size_t(g) * D * sizeof(Elt);
+                    // FP16 rows are read by ldmatrix: swizzle 16-byte chunks by row
+                    const int sc = std::is_same<Elt, __half>::value ? ((c & 8) | ((c & 7) ^ (g & 7))) : c;
+                    reinterpret_cast<float4 *>(dst)[sc] = v;
                 }
                 named_barrier_sync(1, CT);
             }
@@ -567,7 +597,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             else
                 eng.begin(nh, lane, qs);
 
-            for (int t = first; t < npg; t += NC) {
+            for (int t = first; t < npg; t += NSUB) {
                 const int jj = j + t;
                 const int slot = jj % SLOTS;
                 if (stop || flags->abort) break;
@@ -579,7 +609,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
                 if (slot_valid[slot]) {
                     const int lp = sg.y + t;
-                    eng.tile(smem_u32(ring + size_t(slot) * S::TILE_BYTES), min(T, length - lp * T),
+                    eng.tile(smem_u32(ring + size_t(slot) * S::TILE_BYTES), r0, min(T, length - lp * T),
                              a.scale_log2);
                 }
                 __syncwarp();
@@ -588,33 +618,62 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             j += npg;
 
             // ---------------------------------------------------- combine warps
-            eng.store(merge_m + warp * GT, merge_l + warp * GT, merge_o + size_t(warp) * GT * S::OSTRIDE);
-            named_barrier_sync(1, CT);
             const int piece = sg.w;
-            for (int e = ctid; e < nh * D; e += CT) {
-                const int g = e / D, d = e - g * D;
-                float top = -INFINITY;
-#pragma unroll
-                for (int w = 0; w < NC; ++w)
-                    if (merge_l[w * GT + g] > 0.f) top = fmaxf(top, merge_m[w * GT + g]);
-                float den = 0.f, num = 0.f;
-#pragma unroll
-                for (int w = 0; w < NC; ++w) {
-                    const float lw = merge_l[w * GT + g];
-                    if (lw > 0.f) {
-                        const float f = exp2f(merge_m[w * GT + g] - top);
-                        den = fmaf(f, lw, den);
-                        num = fmaf(f, merge_o[(w * GT + g) * S::OSTRIDE + d], num);
+            eng.finish(merge_m + warp * GT, merge_l + warp * GT);
+            if constexpr (NSUB > 1) {
+                float *mo = merge_o + size_t(warp) * GT * S::OSTRIDE;
+                eng.for_each_o([&](int g, int d, float v) { mo[g * S::OSTRIDE + d] = v; });
+            }
+            named_barrier_sync(1, CT);
+            if constexpr (NSUB == 1) {
+                // one warp per KV head: write straight from the accumulators
+                __syncwarp();
+                eng.for_each_o([&](int g, int d, float v) {
+                    if (g >= nh) return;
+                    const float lw = merge_l[warp * GT + g];
+                    if (piece < 0) {
+                        a.out[(qhead0 + g) * D + d] = lw > 0.f ? v / lw : 0.f;
+                    } else {
+                        a.part_o[((int64_t(piece) * HG + hh) * GT + g) * D + d] = v;
+                    }
+                });
+                if (lane < GT && lane < nh) {
+                    const float mw = merge_m[warp * GT + lane], lw = merge_l[warp * GT + lane];
+                    if (piece < 0) {
+                        if (a.stats) reinterpret_cast<float2 *>(a.stats)[qhead0 + lane] = make_float2(mw, lw);
+                    } else {
+                        a.part_ml[(int64_t(piece) * HG + hh) * GT + lane] = make_float2(mw, lw);
                     }
                 }
-                if (piece < 0) {
-                    const int64_t row = int64_t(b) * a.Hq + h0 + g;
-                    a.out[row * D + d] = den > 0.f ? num / den : 0.f;
-                    if (a.stats && d == 0)
-                        reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
-                } else {
-                    a.part_o[(int64_t(piece) * GT + g) * D + d] = num;
-                    if (d == 0) a.part_ml[int64_t(piece) * GT + g] = make_float2(top, den);
+            } else {
+                for (int e = ctid; e < HG * nh * D; e += CT) {
+                    const int h = e / (nh * D), rem = e % (nh * D);
+                    const int g = rem / D, d = rem % D;
+                    float top = -INFINITY;
+#pragma unroll
+                    for (int s = 0; s < NSUB; ++s) {
+                        const int w = s * HG + h;
+                        if (merge_l[w * GT + g] > 0.f) top = fmaxf(top, merge_m[w * GT + g]);
+                    }
+                    float den = 0.f, num = 0.f;
+#pragma unroll
+                    for (int s = 0; s < NSUB; ++s) {
+                        const int w = s * HG + h;
+                        const float lw = merge_l[w * GT + g];
+                        if (lw > 0.f) {
+                            const float f = exp2f(merge_m[w * GT + g] - top);
+                            den = fmaf(f, lw, den);
+                            num = fmaf(f, merge_o[(size_t(w) * GT + g) * S::OSTRIDE + d], num);
+                        }
+                    }
+                    const int64_t row = int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g;
+                    if (piece < 0) {
+                        a.out[row * D + d] = den > 0.f ? num / den : 0.f;
+                        if (a.stats && d == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
+                    } else {
+                        a.part_o[((int64_t(piece) * HG + h) * GT + g) * D + d] = num;
+                        if (d == 0) a.part_ml[(int64_t(piece) * HG + h) * GT + g] = make_float2(top, den);
+                    }
                 }
             }
             if (piece >= 0) {
@@ -629,62 +688,32 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (flags->last) {
                     __threadfence();
                     const int p0 = g1.y, np = g1.z;
-                    for (int e = ctid; e < nh * D; e += CT) {
-                        const int g = e / D, d = e - g * D;
+                    for (int e = ctid; e < HG * nh * D; e += CT) {
+                        const int h = e / (nh * D), rem = e % (nh * D);
+                        const int g = rem / D, d = rem % D;
                         float top = -INFINITY;
                         for (int p = 0; p < np; ++p) {
-                            const float2 ml = __ldcg(a.part_ml + int64_t(p0 + p) * GT + g);
+                            const float2 ml = __ldcg(a.part_ml + (int64_t(p0 + p) * HG + h) * GT + g);
                             if (ml.y > 0.f) top = fmaxf(top, ml.x);
                         }
                         float den = 0.f, num = 0.f;
                         for (int p = 0; p < np; ++p) {
-                            const float2 ml = __ldcg(a.part_ml + int64_t(p0 + p) * GT + g);
+                            const float2 ml = __ldcg(a.part_ml + (int64_t(p0 + p) * HG + h) * GT + g);
                             if (ml.y > 0.f) {
                                 const float f = exp2f(ml.x - top);
                                 den = fmaf(f, ml.y, den);
-                                num = fmaf(f, __ldcg(a.part_o + (int64_t(p0 + p) * GT + g) * D + d), num);
+                                num = fmaf(f, __ldcg(a.part_o + ((int64_t(p0 + p) * HG + h) * GT + g) * D + d), num);
                             }
                         }
-                        const int64_t row = int64_t(b) * a.Hq + h0 + g;
+                        const int64_t row = int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g;
                         a.out[row * D + d] = den > 0.f ? num / den : 0.f;
-                        if (a.stats && d == 0)
-                            reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
+                        if (a.stats && d == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
                     }
                     if (ctid == 0) a.counters[sg.x] = 0;
                 }
             }
             named_barrier_sync(1, CT);
         }
-    }
-}
-
-// ------------------------------------------------------------------ cross-shard merge
-// out[row] = sum_s exp2(m_s - M) * l_s * o_s / sum_s exp2(m_s - M) * l_s over shards
-// with l_s > 0 (o_s is each shard's normalised output); zero when all are empty.
-__global__ void merge_shards_kernel(const float *__restrict__ shard_out,
-                                    const float2 *__restrict__ shard_stats, int shards, int64_t rows,
-                                    int D, float *__restrict__ out) {
-    const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    float top = -INFINITY;
-    for (int s = 0; s < shards; ++s) {
-        const float2 ml = shard_stats[int64_t(s) * rows + row];
-        if (ml.y > 0.f) top = fmaxf(top, ml.x);
-    }
-    float den = 0.f;
-    for (int s = 0; s < shards; ++s) {
-        const float2 ml = shard_stats[int64_t(s) * rows + row];
-        if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
-    }
-    for (int d = lane; d < D; d += 32) {
-        float num = 0.f;
-        for (int s = 0; s < shards; ++s) {
-            const float2 ml = shard_stats[int64_t(s) * rows + row];
-            if (ml.y > 0.f)
-                num = fmaf(exp2f(ml.x - top) * ml.y, shard_out[(int64_t(s) * rows + row) * D + d], num);
-        }
-        out[row * D + d] = den > 0.f ? num / den : 0.f;
     }
 }
 

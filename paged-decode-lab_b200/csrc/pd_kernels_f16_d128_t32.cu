@@ -1,0 +1,4 @@
+// Decode and gather kernels for FP16 inputs, head_dim 128, page_size 32.
+#include "pd_kernels.cuh"
+
+PD_DEFINE_ENTRY(kernel_entry_f16_d128_t32, __half, 128, 32)

@@ -2,22 +2,29 @@
 //
 // The reference plans a rectangular grid [Hq, B, splits] sized by the longest
 // sequence (runtime.py:49, decode.cu:176).  Here the unit of work is a page
-// tile of one group = (sequence, KV head, query-head tile): all G query heads
-// of a KV head share every K/V byte they read.  The total page count over all
-// groups is cut into num_ctas equal contiguous ranges, so each persistent CTA
-// (one per SM) streams the same number of bytes, ragged batches included.
+// tile of one group = (sequence, group of HG KV heads, query-head tile): all
+// G query heads of a KV head share every K/V byte they read, and one TMA box
+// brings a page's rows for HG heads at once.  The total page-tile count over
+// all groups is cut into num_ctas equal contiguous ranges, so each persistent
+// CTA (one per SM) streams the same number of bytes, ragged batches included.
 // A group cut by a range boundary yields one partial per piece; the kernel's
 // last-arriving CTA merges them with the max-corrected merge.
 #include "pd_plan.hpp"
 
+#include "pd_kernels_select.hpp"
+
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 
 namespace pd {
 
 namespace {
 thread_local std::string g_last_error;
+// FP16 page tiles (K + V of HG heads) aim at this size: four TMA boxes of
+// 8 KiB each keep the single issuing thread far ahead of HBM.
+constexpr int kTileTargetBytes = 32 * 1024;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
@@ -98,19 +105,30 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     p.lengths.assign(lengths, lengths + L.batch);
 
     // ---------------------------------------------------------------- groups
+    // A group is (sequence b, KV-head group of HG heads, query-head tile gs):
+    // its page tiles carry HG heads' K and V for one page.
     const int T = L.page_size;
-    const int64_t ngroups = int64_t(L.batch) * L.kv_heads * p.group_splits;
+    // PD_TILE_KIB overrides the FP16 tile target (tuning; capped at 64 KiB).
+    int target = kTileTargetBytes;
+    if (const char *env = std::getenv("PD_TILE_KIB")) {
+        const int kib = std::atoi(env);
+        if (kib >= 1) target = kib * 1024;
+    }
+    const int hg = choose_heads_per_tile(L.head_dim, T, p.group_tile, L.kv_heads, target);
+    p.heads_per_tile = hg;
+    const int kv_groups = L.kv_heads / hg;
+    const int64_t ngroups = int64_t(L.batch) * kv_groups * p.group_splits;
     if (ngroups > INT32_MAX / 2) return fail(PD_ERR_VALUE, "too many (sequence, KV head) groups");
     std::vector<int64_t> gpages(ngroups);
     p.groups.assign(size_t(ngroups) * 8, 0);
     int64_t total = 0;
     for (int b = 0, gi = 0; b < L.batch; ++b)
-        for (int kvh = 0; kvh < L.kv_heads; ++kvh)
+        for (int kg = 0; kg < kv_groups; ++kg)
             for (int gs = 0; gs < p.group_splits; ++gs, ++gi) {
                 int32_t *g = &p.groups[size_t(gi) * 8];
                 g[0] = b;
-                g[1] = kvh;
-                g[2] = kvh * p.group + gs * p.group_tile;
+                g[1] = kg * hg;                        // first KV head of the group
+                g[2] = gs * p.group_tile;              // query-head offset inside each KV head's group
                 g[3] = std::min(p.group_tile, p.group - gs * p.group_tile);
                 g[4] = lengths[b];
                 g[5] = -1;
@@ -187,8 +205,8 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     im.off_groups = off;   off = align256(off + p.groups.size() * 4);
     im.off_counters = off; off = align256(off + size_t(ngroups) * 4);
     im.off_table = off;    off = align256(off + p.table.size() * 4);
-    im.off_part_o = off;   off = align256(off + size_t(pieces) * p.group_tile * L.head_dim * 4);
-    im.off_part_ml = off;  off = align256(off + size_t(pieces) * p.group_tile * 8);
+    im.off_part_o = off;   off = align256(off + size_t(pieces) * hg * p.group_tile * L.head_dim * 4);
+    im.off_part_ml = off;  off = align256(off + size_t(pieces) * hg * p.group_tile * 8);
     im.bytes = off;
     p.host_image.assign(im.off_part_o, 0);
     std::memcpy(p.host_image.data() + im.off_cta, p.cta_off.data(), p.cta_off.size() * 4);

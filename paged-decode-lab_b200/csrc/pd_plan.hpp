@@ -8,7 +8,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/paged_decode.h"
+#include "paged_decode.h"
 
 namespace pd {
 
@@ -41,6 +41,7 @@ struct pd_plan {
     int32_t group = 0;             // G = Hq / Hkv
     int32_t group_tile = 8;        // GT: query heads processed together (8, 16, 32)
     int32_t group_splits = 1;      // ceil(G / GT)
+    int32_t heads_per_tile = 1;    // HG: KV heads gathered per page tile
     int32_t num_ctas = 0;
     int32_t splits = 1;
     int32_t max_context = 0;
@@ -50,7 +51,7 @@ struct pd_plan {
     std::vector<int32_t> lengths;  // [B]
     std::vector<int32_t> cta_off;  // [C + 1]
     std::vector<int32_t> segs;     // 4 per segment
-    std::vector<int32_t> groups;   // 8 per group
+    std::vector<int32_t> groups;   // 8 per group: b, kv0, qoff, nh, length, piece0, npieces, 0
     pd::DeviceImage image;
     std::vector<uint8_t> host_image;  // metadata part of the device buffer
     uint8_t *dev = nullptr;           // bound device buffer (caller-owned)

@@ -26,13 +26,18 @@ def check_worklist(layout, table, lengths, plan):
     G = layout.query_heads // layout.kv_heads
     gt = info["group_tile"]
     assert gt == (8 if G <= 8 else 16 if G <= 16 else 32)
+    hg = info["heads_per_tile"]
+    assert hg in (1, 2, 4, 8) and layout.kv_heads % hg == 0 and hg <= (4 if gt == 32 else 8)
+    # FP16 page tile (K + V of hg heads) within the 32 KiB target unless hg == 1
+    assert hg == 1 or hg * 2 * layout.head_dim * 2 * T <= 32 * 1024
     splits = math.ceil(G / gt)
-    assert info["num_groups"] == layout.batch * layout.kv_heads * splits
-    # groups enumerate (b, kvh, head tile) in order
+    kv_groups = layout.kv_heads // hg
+    assert info["num_groups"] == layout.batch * kv_groups * splits
+    # groups enumerate (b, KV-head group, query-head tile) in order
     for gi, g in enumerate(groups):
-        b, rest = divmod(gi, layout.kv_heads * splits)
-        kvh, s = divmod(rest, splits)
-        assert tuple(g[:5]) == (b, kvh, kvh * G + s * gt, min(gt, G - s * gt), lengths[b])
+        b, rest = divmod(gi, kv_groups * splits)
+        kg, s = divmod(rest, splits)
+        assert tuple(g[:5]) == (b, kg * hg, s * gt, min(gt, G - s * gt), lengths[b])
     C = info["num_ctas"]
     assert offs[0] == 0 and offs[-1] == len(segs) and (np.diff(offs) >= 0).all()
     total = sum(-(-int(lengths[g[0]]) // T) for g in groups)
@@ -66,10 +71,10 @@ def check_worklist(layout, table, lengths, plan):
 
 
 @pytest.mark.parametrize("ctas", [1, 2, 3, 7, 64, 148, 1000])
-@pytest.mark.parametrize("kv_heads,heads", [(2, 8), (1, 32), (4, 4), (1, 64), (2, 24)])
+@pytest.mark.parametrize("kv_heads,heads", [(2, 8), (1, 32), (4, 4), (1, 64), (2, 24), (8, 32), (6, 12)])
 def test_worklist_invariants_small(ctas, kv_heads, heads):
     rng = np.random.default_rng(ctas * 31 + heads)
-    layout = Layout(5, heads, kv_heads, 64, 16, 60)
+    layout = Layout(5, heads, kv_heads, 64 if heads % 3 else 128, 16, 60)
     lengths = np.array([0, 1, 17, 160, 191], dtype=np.int32)
     table = rng.integers(0, 60, size=(5, 12)).astype(np.int32)
     plan = inspect_plan(layout, table, lengths, split_tokens=33, num_ctas=ctas)
@@ -114,3 +119,11 @@ def test_plan_errors_mirror_reference_messages():
         inspect_plan(layout, [[0, 9]], [17])
     with pytest.raises(TypeError):
         inspect_plan(layout, [[0.0, 1.0]], [17])
+
+
+@pytest.mark.parametrize("dim,page,kv_heads,expected", [
+    (128, 16, 8, 4), (128, 32, 8, 2), (64, 16, 8, 8), (64, 32, 32, 4), (128, 32, 1, 1), (128, 16, 6, 2)])
+def test_heads_per_tile_targets_32kib_fp16_tiles(dim, page, kv_heads, expected):
+    layout = Layout(2, kv_heads * 4, kv_heads, dim, page, 8)
+    plan = inspect_plan(layout, np.arange(8, dtype=np.int32).reshape(2, 4), [page * 4, 1], num_ctas=3)
+    assert plan["info"]["heads_per_tile"] == expected

@@ -313,7 +313,7 @@ def run_ours(args, rank, local, world):
                      "traffic": traffic, "kernel": "paged_decode_kernel",
                      "kernel_us": kernel_ms * 1e3,
                      "algorithmic_bytes_per_launch": nbytes},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * plan.kernels_per_run,
         "clocks": clocks.summary(),
     }
     if e2e:

@@ -70,7 +70,8 @@ typedef struct pd_plan_info {
     int32_t num_ctas;        /* persistent CTAs the decode kernel launches */
     int32_t num_segments;    /* (group, page range) work segments over all CTAs */
     int32_t num_groups;      /* (sequence, KV-head group, query-head tile) groups */
-    int32_t num_pieces;      /* segments of groups that span >1 CTA: partials to merge */
+    int32_t num_pieces;      /* partial slots written by the decode kernel and merged after it */
+    int32_t slot_stride;     /* partial slots reserved per segment (one per consumer sub-pipeline) */
     int32_t group_tile;      /* query heads per group tile (8, 16 or 32) */
     int32_t heads_per_tile;  /* KV heads gathered per page tile (1, 2, 4 or 8) */
     int32_t total_pages;     /* page tiles streamed per decode (all groups) */
@@ -82,7 +83,8 @@ typedef struct pd_plan_info {
  * split planning (runtime.py:32-69) and decode_cuda's validation
  * (decode.cu:201-237).  Copies table and lengths.  merge_mode 0 = "serial",
  * 1 = "shared" is accepted for API compatibility (runtime.py:33-34); the
- * kernel always uses its fused merge.  device < 0 builds a host-only plan
+ * decode always merges split partials the same way (a dependent merge kernel
+ * launched right behind the decode kernel).  device < 0 builds a host-only plan
  * (inspection, no decode).  num_ctas <= 0 picks one CTA per SM of device.
  */
 pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
@@ -94,10 +96,11 @@ void pd_plan_destroy(pd_plan *plan);
 pd_status pd_plan_get_info(const pd_plan *plan, pd_plan_info *info);
 
 /* Work list, for inspection and tests: segments as int32 quadruples
- * (group, first_page, end_page, piece or -1), groups as int32 octuples
- * (batch, first_kv_head, query_head_offset, query_heads, length, first_piece,
- * pieces, 0): the group covers heads_per_tile KV heads from first_kv_head and,
- * of each one's G query heads, query_heads of them from query_head_offset;
+ * (group, first_page, end_page, first partial slot or -1), groups as int32
+ * octuples (batch, first_kv_head, query_head_offset, query_heads, length,
+ * first partial slot or -1, segments, 0): the group covers heads_per_tile KV
+ * heads from first_kv_head and, of each one's G query heads, query_heads of
+ * them from query_head_offset; slot -1 means the output is written directly;
  * cta_offsets receives the per-CTA segment offsets [num_ctas + 1].  Any
  * pointer may be NULL.
  */
@@ -115,7 +118,8 @@ pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *s
 
 /* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
  * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
- * k and v must be 16-byte aligned (TMA).  Asynchronous on `stream`.
+ * k and v must be 16-byte aligned (TMA).  Asynchronous on `stream`: one
+ * decode kernel, plus a merge kernel when the plan has partial slots.
  */
 pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
                     float *out, void *stream);

@@ -120,7 +120,6 @@ DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
     a.cta_off = reinterpret_cast<const int32_t *>(dev + im.off_cta);
     a.segs = reinterpret_cast<const int4 *>(dev + im.off_segs);
     a.groups = reinterpret_cast<const int4 *>(dev + im.off_groups);
-    a.counters = reinterpret_cast<int32_t *>(dev + im.off_counters);
     a.part_o = reinterpret_cast<float *>(dev + im.off_part_o);
     a.part_ml = reinterpret_cast<float2 *>(dev + im.off_part_ml);
     a.out = out;
@@ -131,6 +130,8 @@ DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
     a.W = int32_t(p->width);
     a.max_len = p->max_context;
     a.group = p->group;
+    a.slot_stride = p->slot_stride;
+    a.num_groups = int32_t(p->groups.size() / 8);
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
@@ -155,11 +156,16 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
         kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode);
     pd_status s = ensure_smem_attribute(p->device, e);
     if (s != PD_OK) return s;
-    e.fn<<<p->num_ctas, e.threads, e.smem, static_cast<cudaStream_t>(stream)>>>(tc.map_k, tc.map_v,
-                                                                              args);
-    const cudaError_t err = cudaGetLastError();
+    const auto st = static_cast<cudaStream_t>(stream);
+    e.fn<<<p->num_ctas, e.threads, e.smem, st>>>(tc.map_k, tc.map_v, args);
+    cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
+    if (mode == kModeDecode && p->num_pieces > 0) {
+        err = launch_merge_partials(args, p->heads_per_tile, p->group_tile, e.nsub, p->layout.head_dim, st);
+        if (err != cudaSuccess)
+            return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
+    }
     return PD_OK;
 }
 
@@ -221,9 +227,9 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->num_pieces = p->num_pieces;
     info->group_tile = p->group_tile;
     info->heads_per_tile = p->heads_per_tile;
+    info->slot_stride = p->slot_stride;
     info->total_pages = int32_t(p->total_pages);
-    info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o) +
-                            int64_t(p->groups.size() / 8) * 4;
+    info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o);
     info->device_bytes = int64_t(p->image.bytes);
     return PD_OK;
 }

@@ -20,10 +20,11 @@
 //     query heads of that KV head at once: FP16 inputs use m16n8k16
 //     tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T, FP32 accumulators), FP32
 //     inputs use FP32 FMAs;
-//   * at a segment's end the NSUB warps of each KV head combine their states
-//     through shared memory; a group owned by one CTA writes its normalised
-//     output directly, otherwise each CTA writes an (m, l, o) partial and the
-//     CTA that arrives last (atomic counter, reset after use) merges them.
+//   * consumer warps never wait for each other: at the end of its share of
+//     a segment a warp writes its heads' normalised output directly when it
+//     alone saw the whole group (one segment, NSUB == 1), else an (m, l, o)
+//     partial; a small merge kernel, launched programmatically dependent on
+//     this one (PDL), combines the partials with the max-corrected merge.
 //
 // All exponentials are base 2 on scores pre-multiplied by log2(e)/sqrt(D);
 // this is the reference's exp(s - m) rewritten, not a different softmax.
@@ -39,17 +40,18 @@ struct DecodeArgs {
     const void *q;            // [B, Hq, D] in the input dtype
     const int32_t *table;     // [B, W]
     const int32_t *cta_off;   // [C + 1] segment range of each CTA
-    const int4 *segs;         // {group, first_page, end_page, piece (-1: sole piece)}
-    const int4 *groups;       // 2 per group: {b, kv_head0, q_head_offset, nh}, {length, piece0, npieces, 0}
-    int32_t *counters;        // [groups] arrivals of multi-piece groups (self-resetting)
-    float *part_o;            // [pieces, HG, GT, D] unnormalised partial outputs
-    float2 *part_ml;          // [pieces, HG, GT] (m, l) of each partial
+    const int4 *segs;         // {group, first_page, end_page, slot (-1: write output directly)}
+    const int4 *groups;       // 2 per group: {b, kv_head0, q_head_offset, nh}, {length, slot0, segments, 0}
+    float *part_o;            // [slots, HG, GT, D] unnormalised partial outputs
+    float2 *part_ml;          // [slots, HG, GT] (m, l) of each partial
     float *out;               // [B, Hq, D]
     float *stats;             // [B, Hq, 2] (m, l) or nullptr
     uint32_t *error;          // error word (PD_DEVERR_* bits)
     void *dense_k;            // gather mode: [B, Hkv, max_len, D]
     void *dense_v;
     int32_t Hq, Hkv, W, max_len, group;   // group = G = Hq / Hkv
+    int32_t slot_stride;      // partial slots reserved per segment (>= NSUB)
+    int32_t num_groups;
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
 };
@@ -67,24 +69,20 @@ struct KernelShape {
     static constexpr int ROWS = HG * T;                // swizzle rows per box: [head][token]
     static constexpr int HALF_BYTES = NBOX * ROWS * 128;  // K (or V) part of one page tile
     static constexpr int TILE_BYTES = 2 * HALF_BYTES;
-    static constexpr int OSTRIDE = D + 4;              // padded merge rows: conflict-free stores
     static constexpr int THREADS = (NC + 1) * 32;
     static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
-    static constexpr size_t MERGE_O = NSUB > 1 ? size_t(NC) * GT * OSTRIDE * 4 : 0;
-    static constexpr size_t MERGE_ML = size_t(NC) * GT * 2 * 4;
     // FP16 with up to 16 query heads per KV head keeps Q in registers;
-    // otherwise Q of all HG heads is staged in shared memory per segment.
+    // otherwise every consumer warp stages its heads' Q in its own slice.
     static constexpr bool Q_SMEM = !(ELT == 2 && GT <= 16);
-    static constexpr size_t QS = Q_SMEM ? size_t(HG) * GT * D * ELT : 0;
+    static constexpr size_t QS = Q_SMEM ? size_t(NC) * GT * D * ELT : 0;
     static constexpr size_t BARS = size_t(SLOTS) * 16;
     static constexpr size_t FLAGS = size_t(SLOTS) * 4 + 16;
-    static constexpr size_t SMEM = 1024 + RING + MERGE_O + MERGE_ML + QS + BARS + FLAGS;
+    static constexpr size_t SMEM = 1024 + RING + QS + BARS + FLAGS;
 };
 
 struct SmemFlags {
     volatile int abort;
-    int last;
-    int pad[2];
+    int pad[3];
 };
 
 // ------------------------------------------------------------------ FP16 tensor-core engine
@@ -252,26 +250,17 @@ struct HalfEngine {
         }
     }
 
-    // Reduce l over the lanes sharing a query head; publish m and l (lanes 0-3).
-    __device__ __forceinline__ void finish(float *sm_m, float *sm_l) {
+    // Sum l over the 8 lanes that share each query head (lane & 3 picks the head pair).
+    __device__ __forceinline__ void reduce() {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
                 for (int s = 4; s < 32; s <<= 1) l[nt][i] += __shfl_xor_sync(kFullMask, l[nt][i], s);
-        if (lane < 4) {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    sm_m[nt * 8 + 2 * lane + i] = m[nt][i];
-                    sm_l[nt * 8 + 2 * lane + i] = l[nt][i];
-                }
-        }
     }
 
-    // Call f(g, d, value) for every accumulator element this lane holds.
+    // f(g, d, o, m, l) for every accumulator element this lane holds.
     template <typename F>
     __device__ __forceinline__ void for_each_o(F &&f) const {
 #pragma unroll
@@ -280,11 +269,22 @@ struct HalfEngine {
             for (int nt = 0; nt < NT; ++nt) {
                 const int g = nt * 8 + 2 * (lane & 3);
                 const int d = dt * 16 + (lane >> 2);
-                f(g, d, acc[dt][nt][0]);
-                f(g + 1, d, acc[dt][nt][1]);
-                f(g, d + 8, acc[dt][nt][2]);
-                f(g + 1, d + 8, acc[dt][nt][3]);
+                f(g, d, acc[dt][nt][0], m[nt][0], l[nt][0]);
+                f(g + 1, d, acc[dt][nt][1], m[nt][1], l[nt][1]);
+                f(g, d + 8, acc[dt][nt][2], m[nt][0], l[nt][0]);
+                f(g + 1, d + 8, acc[dt][nt][3], m[nt][1], l[nt][1]);
             }
+    }
+
+    // f(g, m, l) once per query head (lanes 0-3).
+    template <typename F>
+    __device__ __forceinline__ void for_each_ml(F &&f) const {
+        if (lane < 4) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) f(nt * 8 + 2 * lane + i, m[nt][i], l[nt][i]);
+        }
     }
 };
 
@@ -383,17 +383,11 @@ struct FloatEngine {
         }
     }
 
-    __device__ __forceinline__ void finish(float *sm_m, float *sm_l) {
+    __device__ __forceinline__ void reduce() {
 #pragma unroll
         for (int g = 0; g < GT; ++g) {
-            float s = l[g];
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) s += __shfl_xor_sync(kFullMask, s, o);
-            l[g] = s;
-            if (lane == 0) {
-                sm_m[g] = m[g];
-                sm_l[g] = s;
-            }
+            for (int o = 1; o < 32; o <<= 1) l[g] += __shfl_xor_sync(kFullMask, l[g], o);
         }
     }
 
@@ -402,7 +396,15 @@ struct FloatEngine {
 #pragma unroll
         for (int g = 0; g < GT; ++g)
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) f(g, lane * DPL + i, acc[g][i]);
+            for (int i = 0; i < DPL; ++i) f(g, lane * DPL + i, acc[g][i], m[g], l[g]);
+    }
+
+    template <typename F>
+    __device__ __forceinline__ void for_each_ml(F &&f) const {
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < GT; ++g) f(g, m[g], l[g]);
+        }
     }
 };
 
@@ -438,10 +440,7 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
-    float *merge_o = reinterpret_cast<float *>(ring + S::RING);
-    float *merge_m = merge_o + S::MERGE_O / 4;
-    float *merge_l = merge_m + size_t(NC) * GT;
-    uint8_t *qsm = reinterpret_cast<uint8_t *>(merge_l + size_t(NC) * GT);
+    uint8_t *qsm = ring + S::RING;
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(qsm + S::QS);
     uint64_t *empty_bar = full_bar + SLOTS;
     int *slot_valid = reinterpret_cast<int *>(empty_bar + SLOTS);
@@ -458,7 +457,6 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
             mbar_init(smem_u32(empty_bar + s), HG);   // released by the HG warps that read it
         }
         flags->abort = 0;
-        flags->last = 0;
         mbar_init_fence();
     }
     __syncthreads();
@@ -516,8 +514,6 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
     }
 
     // ---------------------------------------------------------------- consumers
-    constexpr int CT = NC * 32;
-    const int ctid = threadIdx.x;
     const int hh = warp % HG;       // KV head of the group this warp owns
     const int sub = warp / HG;      // this warp takes tiles j with j % NSUB == sub
     const int r0 = hh * T;          // its rows in a [head][token] tile
@@ -537,60 +533,54 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
             for (int t = first; t < npg; t += NSUB) {
                 const int jj = j + t;
                 const int slot = jj % SLOTS;
-                if (!stop && !flags->abort) {
-                    if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
-                        if (lane == 0) atomicOr(a.error, kErrTimeout);
-                        flags->abort = 1;
-                        stop = true;
-                    } else {
-                        const int lp = sg.y + t;
-                        const int valid = min(T, length - lp * T);
-                        if (slot_valid[slot]) {
-                            const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
-                            const int64_t base = (int64_t(b) * a.Hkv + kv0 + hh) * a.max_len + int64_t(lp) * T;
-                            for (int idx = lane; idx < valid * CPR; idx += 32) {
-                                const int r = idx / CPR, c = idx % CPR;
-                                const float4 kv = lds_f4(kb + swz128<S::ROWS>(r0 + r, c));
-                                const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<S::ROWS>(r0 + r, c));
-                                const int64_t off = (base + r) * S::ROW_BYTES + c * 16;
-                                *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_k) + off) = kv;
-                                *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_v) + off) = vv;
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(smem_u32(empty_bar + slot));
+                if (stop || flags->abort) break;
+                if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
+                    if (lane == 0) atomicOr(a.error, kErrTimeout);
+                    flags->abort = 1;
+                    stop = true;
+                    break;
+                }
+                const int lp = sg.y + t;
+                const int valid = min(T, length - lp * T);
+                if (slot_valid[slot]) {
+                    const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+                    const int64_t base = (int64_t(b) * a.Hkv + kv0 + hh) * a.max_len + int64_t(lp) * T;
+                    for (int idx = lane; idx < valid * CPR; idx += 32) {
+                        const int r = idx / CPR, c = idx % CPR;
+                        const float4 kv = lds_f4(kb + swz128<S::ROWS>(r0 + r, c));
+                        const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<S::ROWS>(r0 + r, c));
+                        const int64_t off = (base + r) * S::ROW_BYTES + c * 16;
+                        *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_k) + off) = kv;
+                        *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_v) + off) = vv;
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(empty_bar + slot));
             }
             j += npg;
-            continue;
         } else {
             using Engine = typename EngineFor<Elt, D, T, GT, S::ROWS>::type;
             Engine eng;
             // query heads of this warp's KV head: (kv0 + hh) * G + qoff + g, g < nh
             const int64_t qhead0 = int64_t(b) * a.Hq + int64_t(kv0 + hh) * a.group + qoff;
             const Elt *qrow = static_cast<const Elt *>(a.q) + qhead0 * D;
-            uint8_t *qmine = qsm + size_t(hh) * GT * D * sizeof(Elt);
+            uint8_t *qmine = qsm + size_t(warp) * GT * D * sizeof(Elt);
             const uint32_t qs = smem_u32(qmine);
             static_assert(!std::is_same<Elt, __half>::value ||
                               S::Q_SMEM == !HalfEngine<D, T, GT, S::ROWS>::Q_REGS,
                           "Q staging must match the FP16 engine");
             if constexpr (S::Q_SMEM) {
-                // cooperative Q load for all HG heads (zero rows for heads past nh)
-                for (int e = ctid; e < HG * GT * (D * int(sizeof(Elt)) / 16); e += CT) {
-                    const int per_head = GT * (D * int(sizeof(Elt)) / 16);
-                    const int h = e / per_head, r = e % per_head;
-                    const int g = r / (D * int(sizeof(Elt)) / 16), c = r % (D * int(sizeof(Elt)) / 16);
-                    const Elt *src = static_cast<const Elt *>(a.q) +
-                                     (int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g) * D;
+                // this warp's Q rows (zero rows for heads past nh) into its own slice
+                constexpr int CPR = D * int(sizeof(Elt)) / 16;
+                for (int e = lane; e < GT * CPR; e += 32) {
+                    const int g = e / CPR, c = e % CPR;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (g < nh) v = reinterpret_cast<const float4 *>(src)[c];
-                    uint8_t *dst = qsm + size_t(h) * GT * D * sizeof(Elt) + size_t(g) * D * sizeof(Elt);
+                    if (g < nh) v = __ldg(reinterpret_cast<const float4 *>(qrow + int64_t(g) * D) + c);
                     // FP16 rows are read by ldmatrix: swizzle 16-byte chunks by row
                     const int sc = std::is_same<Elt, __half>::value ? ((c & 8) | ((c & 7) ^ (g & 7))) : c;
-                    reinterpret_cast<float4 *>(dst)[sc] = v;
+                    reinterpret_cast<float4 *>(qmine + size_t(g) * D * sizeof(Elt))[sc] = v;
                 }
-                named_barrier_sync(1, CT);
+                __syncwarp();
             }
             if constexpr (std::is_same<Elt, __half>::value)
                 eng.begin(reinterpret_cast<const __half *>(qrow), nh, lane, qs);
@@ -617,104 +607,88 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
             }
             j += npg;
 
-            // ---------------------------------------------------- combine warps
-            const int piece = sg.w;
-            eng.finish(merge_m + warp * GT, merge_l + warp * GT);
-            if constexpr (NSUB > 1) {
-                float *mo = merge_o + size_t(warp) * GT * S::OSTRIDE;
-                eng.for_each_o([&](int g, int d, float v) { mo[g * S::OSTRIDE + d] = v; });
-            }
-            named_barrier_sync(1, CT);
-            if constexpr (NSUB == 1) {
-                // one warp per KV head: write straight from the accumulators
-                __syncwarp();
-                eng.for_each_o([&](int g, int d, float v) {
-                    if (g >= nh) return;
-                    const float lw = merge_l[warp * GT + g];
-                    if (piece < 0) {
-                        a.out[(qhead0 + g) * D + d] = lw > 0.f ? v / lw : 0.f;
-                    } else {
-                        a.part_o[((int64_t(piece) * HG + hh) * GT + g) * D + d] = v;
-                    }
+            // ---------------------------------------------------- publish this warp's state
+            eng.reduce();
+            if (sg.w < 0) {
+                // the group's only segment and the only warp of this head: final output
+                eng.for_each_o([&](int g, int d, float o, float, float l) {
+                    if (g < nh) a.out[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
                 });
-                if (lane < GT && lane < nh) {
-                    const float mw = merge_m[warp * GT + lane], lw = merge_l[warp * GT + lane];
-                    if (piece < 0) {
-                        if (a.stats) reinterpret_cast<float2 *>(a.stats)[qhead0 + lane] = make_float2(mw, lw);
-                    } else {
-                        a.part_ml[(int64_t(piece) * HG + hh) * GT + lane] = make_float2(mw, lw);
-                    }
-                }
+                if (a.stats)
+                    eng.for_each_ml([&](int g, float m, float l) {
+                        if (g < nh) reinterpret_cast<float2 *>(a.stats)[qhead0 + g] = make_float2(m, l);
+                    });
             } else {
-                for (int e = ctid; e < HG * nh * D; e += CT) {
-                    const int h = e / (nh * D), rem = e % (nh * D);
-                    const int g = rem / D, d = rem % D;
-                    float top = -INFINITY;
-#pragma unroll
-                    for (int s = 0; s < NSUB; ++s) {
-                        const int w = s * HG + h;
-                        if (merge_l[w * GT + g] > 0.f) top = fmaxf(top, merge_m[w * GT + g]);
-                    }
-                    float den = 0.f, num = 0.f;
-#pragma unroll
-                    for (int s = 0; s < NSUB; ++s) {
-                        const int w = s * HG + h;
-                        const float lw = merge_l[w * GT + g];
-                        if (lw > 0.f) {
-                            const float f = exp2f(merge_m[w * GT + g] - top);
-                            den = fmaf(f, lw, den);
-                            num = fmaf(f, merge_o[(size_t(w) * GT + g) * S::OSTRIDE + d], num);
-                        }
-                    }
-                    const int64_t row = int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g;
-                    if (piece < 0) {
-                        a.out[row * D + d] = den > 0.f ? num / den : 0.f;
-                        if (a.stats && d == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
-                    } else {
-                        a.part_o[((int64_t(piece) * HG + h) * GT + g) * D + d] = num;
-                        if (d == 0) a.part_ml[(int64_t(piece) * HG + h) * GT + g] = make_float2(top, den);
-                    }
-                }
+                const int64_t ps = (int64_t(sg.w) + sub) * HG + hh;   // [slot][head] partial row
+                eng.for_each_o([&](int g, int d, float o, float, float) {
+                    if (g < nh) a.part_o[(ps * GT + g) * D + d] = o;
+                });
+                eng.for_each_ml([&](int g, float m, float l) {
+                    if (g < nh) a.part_ml[ps * GT + g] = make_float2(m, l);
+                });
             }
-            if (piece >= 0) {
-                // last-arriving CTA of the group merges all its partials
-                __threadfence();
-                named_barrier_sync(1, CT);
-                if (ctid == 0) {
-                    const int prev = atomicAdd(a.counters + sg.x, 1);
-                    flags->last = (prev == g1.z - 1);
-                }
-                named_barrier_sync(1, CT);
-                if (flags->last) {
-                    __threadfence();
-                    const int p0 = g1.y, np = g1.z;
-                    for (int e = ctid; e < HG * nh * D; e += CT) {
-                        const int h = e / (nh * D), rem = e % (nh * D);
-                        const int g = rem / D, d = rem % D;
-                        float top = -INFINITY;
-                        for (int p = 0; p < np; ++p) {
-                            const float2 ml = __ldcg(a.part_ml + (int64_t(p0 + p) * HG + h) * GT + g);
-                            if (ml.y > 0.f) top = fmaxf(top, ml.x);
-                        }
-                        float den = 0.f, num = 0.f;
-                        for (int p = 0; p < np; ++p) {
-                            const float2 ml = __ldcg(a.part_ml + (int64_t(p0 + p) * HG + h) * GT + g);
-                            if (ml.y > 0.f) {
-                                const float f = exp2f(ml.x - top);
-                                den = fmaf(f, ml.y, den);
-                                num = fmaf(f, __ldcg(a.part_o + ((int64_t(p0 + p) * HG + h) * GT + g) * D + d), num);
-                            }
-                        }
-                        const int64_t row = int64_t(b) * a.Hq + int64_t(kv0 + h) * a.group + qoff + g;
-                        a.out[row * D + d] = den > 0.f ? num / den : 0.f;
-                        if (a.stats && d == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
-                    }
-                    if (ctid == 0) a.counters[sg.x] = 0;
-                }
-            }
-            named_barrier_sync(1, CT);
         }
     }
+    // Let the dependent merge kernel launch; it still waits for this grid to finish.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ partial merge
+// One warp per (group, KV head of the group, query head g): max-corrected merge
+// (oracle.py:88-96 algebra) of the partials written by `nsub` sub-pipelines
+// over each of the group's segments.  Launched programmatically dependent on
+// the decode kernel: griddepcontrol.wait returns once that grid has finished
+// and its writes are visible.
+template <int HG, int GT>
+__global__ void __launch_bounds__(128) merge_partials_kernel(const DecodeArgs a, int nsub, int D) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t wid = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = int64_t(a.num_groups) * HG * GT;
+    if (wid >= rows) return;
+    const int gi = int(wid / (HG * GT));
+    const int hh = int(wid / GT % HG);
+    const int g = int(wid % GT);
+    const int4 g0 = a.groups[2 * gi];
+    const int4 g1 = a.groups[2 * gi + 1];
+    if (g1.y < 0 || g >= g0.w) return;         // written directly, or a padding head
+    const int parts = g1.z * nsub;
+    auto slot_of = [&](int p) { return int64_t(g1.y) + int64_t(p / nsub) * a.slot_stride + p % nsub; };
+    float top = -INFINITY;
+    for (int p = lane; p < parts; p += 32) {
+        const float2 ml = a.part_ml[(slot_of(p) * HG + hh) * GT + g];
+        if (ml.y > 0.f) top = fmaxf(top, ml.x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(kFullMask, top, o));
+    float den = 0.f;
+    for (int p = lane; p < parts; p += 32) {
+        const float2 ml = a.part_ml[(slot_of(p) * HG + hh) * GT + g];
+        if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(kFullMask, den, o);
+    const int64_t row = int64_t(g0.x) * a.Hq + int64_t(g0.y + hh) * a.group + g0.z + g;
+    for (int d0 = lane * 4; d0 < D; d0 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int p = 0; p < parts; ++p) {
+            const int64_t pr = slot_of(p) * HG + hh;
+            const float2 ml = a.part_ml[pr * GT + g];
+            if (ml.y > 0.f) {
+                const float w = exp2f(ml.x - top);
+                const float4 o = *reinterpret_cast<const float4 *>(a.part_o + (pr * GT + g) * D + d0);
+                acc.x = fmaf(w, o.x, acc.x);
+                acc.y = fmaf(w, o.y, acc.y);
+                acc.z = fmaf(w, o.z, acc.z);
+                acc.w = fmaf(w, o.w, acc.w);
+            }
+        }
+        *reinterpret_cast<float4 *>(a.out + row * D + d0) =
+            den > 0.f ? make_float4(acc.x / den, acc.y / den, acc.z / den, acc.w / den)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
 }
 
 }  // namespace pd

@@ -18,6 +18,7 @@ struct KernelEntry {
     size_t smem;
     int consumers;
     int slots;
+    int nsub;       // sub-pipelines: partial slots each segment's warps write
 };
 
 // Shape of one kernel: HG KV heads per page tile and NSUB sub-pipelines of
@@ -61,7 +62,7 @@ KernelEntry make_entry() {
     using L = LaunchShape<Elt, D, T, GT, HG>;
     using S = KernelShape<Elt, D, T, GT, HG, L::NSUB, L::SLOTS>;
     return {&paged_decode_kernel<Elt, D, T, GT, HG, L::NSUB, L::SLOTS, MODE>, S::THREADS, S::SMEM, S::NC,
-            L::SLOTS};
+            L::SLOTS, L::NSUB};
 }
 
 // KV heads per tile are instantiated while an FP16 page tile (K + V of HG
@@ -93,6 +94,11 @@ KernelEntry entry_for(int gt, int hg) {
     if (gt == 16) return entry_for_hg<Elt, D, T, 16, MODE>(hg);
     return entry_for_hg<Elt, D, T, 32, MODE>(hg);
 }
+
+// Merge of the decode kernel's partials, launched programmatically dependent
+// on it (PDL) on the same stream (pd_merge.cu).
+cudaError_t launch_merge_partials(const DecodeArgs &args, int hg, int gt, int nsub, int D,
+                                  cudaStream_t stream);
 
 // Max-corrected merge of [shards, rows, D] shard outputs (pd_merge.cu).
 cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t rows,

@@ -34,6 +34,40 @@ static __global__ void merge_shards_kernel(const float *__restrict__ shard_out,
 }
 
 
+template <int HG, int GT>
+static cudaError_t launch_merge(const DecodeArgs &args, int nsub, int D, cudaStream_t stream) {
+    const int64_t warps = int64_t(args.num_groups) * HG * GT;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned((warps + 3) / 4));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, merge_partials_kernel<HG, GT>, args, nsub, D);
+}
+
+cudaError_t launch_merge_partials(const DecodeArgs &args, int hg, int gt, int nsub, int D,
+                                  cudaStream_t stream) {
+    switch (gt * 16 + hg) {
+        case 8 * 16 + 1: return launch_merge<1, 8>(args, nsub, D, stream);
+        case 8 * 16 + 2: return launch_merge<2, 8>(args, nsub, D, stream);
+        case 8 * 16 + 4: return launch_merge<4, 8>(args, nsub, D, stream);
+        case 8 * 16 + 8: return launch_merge<8, 8>(args, nsub, D, stream);
+        case 16 * 16 + 1: return launch_merge<1, 16>(args, nsub, D, stream);
+        case 16 * 16 + 2: return launch_merge<2, 16>(args, nsub, D, stream);
+        case 16 * 16 + 4: return launch_merge<4, 16>(args, nsub, D, stream);
+        case 16 * 16 + 8: return launch_merge<8, 16>(args, nsub, D, stream);
+        case 32 * 16 + 1: return launch_merge<1, 32>(args, nsub, D, stream);
+        case 32 * 16 + 2: return launch_merge<2, 32>(args, nsub, D, stream);
+        case 32 * 16 + 4: return launch_merge<4, 32>(args, nsub, D, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t rows,
                                 int D, float *out, cudaStream_t stream) {
     constexpr int kRowsPerBlock = 8;

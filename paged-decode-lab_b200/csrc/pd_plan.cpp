@@ -7,8 +7,9 @@
 // brings a page's rows for HG heads at once.  The total page-tile count over
 // all groups is cut into num_ctas equal contiguous ranges, so each persistent
 // CTA (one per SM) streams the same number of bytes, ragged batches included.
-// A group cut by a range boundary yields one partial per piece; the kernel's
-// last-arriving CTA merges them with the max-corrected merge.
+// A group cut by range boundaries is seen in pieces; each piece's warps
+// write (m, l, o) partials that a small dependent kernel merges with the
+// max-corrected merge.
 #include "pd_plan.hpp"
 
 #include "pd_kernels_select.hpp"
@@ -168,29 +169,40 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         }
         cursor = end;
     }
-    // pieces: a group with more than one segment gets consecutive partial slots
-    std::vector<int32_t> next_piece(ngroups, -1);
-    int32_t pieces = 0;
+    // Partial slots.  A segment's consumer warps run as NSUB sub-pipelines
+    // (NSUB <= NC0 / HG, fewer when a kernel's tiles leave room for fewer
+    // slots), each writing its own partial; slot_stride = NC0 / HG slots are
+    // reserved per segment.  A group with one segment and slot_stride == 1 is
+    // seen whole by one warp per head, which writes the final output itself.
+    const int nc0 = p.group_tile == 32 ? 4 : 8;
+    p.slot_stride = std::max(1, nc0 / hg);
+    std::vector<int32_t> next_slot(ngroups, -1);
+    int64_t slots = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) {
         int32_t *g = &p.groups[size_t(gi) * 8];
-        if (seg_count[gi] > 1) {
-            g[5] = pieces;
-            g[6] = seg_count[gi];
-            next_piece[gi] = pieces;
-            pieces += seg_count[gi];
-        } else {
+        g[6] = seg_count[gi];
+        if (seg_count[gi] == 1 && p.slot_stride == 1) {
             g[5] = -1;
-            g[6] = 1;
+        } else {
+            g[5] = int32_t(slots);
+            next_slot[gi] = int32_t(slots);
+            slots += int64_t(seg_count[gi]) * p.slot_stride;
         }
     }
-    p.num_pieces = pieces;
+    if (slots > INT32_MAX / 64) return fail(PD_ERR_VALUE, "too many partial slots");
+    p.num_pieces = int32_t(slots);
     p.cta_off.assign(size_t(C) + 1, 0);
     p.segs.clear();
     for (int64_t i = 0; i < C; ++i) {
         for (size_t k = 0; k < per[i].size(); k += 4) {
-            int32_t *s = &per[i][k];
-            const int32_t gi = s[0];
-            s[3] = seg_count[gi] > 1 ? next_piece[gi]++ : -1;
+            int32_t *sv = &per[i][k];
+            const int32_t gi = sv[0];
+            if (next_slot[gi] < 0) {
+                sv[3] = -1;
+            } else {
+                sv[3] = next_slot[gi];
+                next_slot[gi] += p.slot_stride;
+            }
         }
         p.segs.insert(p.segs.end(), per[i].begin(), per[i].end());
         p.cta_off[i + 1] = int32_t(p.segs.size() / 4);
@@ -203,10 +215,9 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     im.off_cta = off;      off = align256(off + p.cta_off.size() * 4);
     im.off_segs = off;     off = align256(off + p.segs.size() * 4);
     im.off_groups = off;   off = align256(off + p.groups.size() * 4);
-    im.off_counters = off; off = align256(off + size_t(ngroups) * 4);
     im.off_table = off;    off = align256(off + p.table.size() * 4);
-    im.off_part_o = off;   off = align256(off + size_t(pieces) * hg * p.group_tile * L.head_dim * 4);
-    im.off_part_ml = off;  off = align256(off + size_t(pieces) * hg * p.group_tile * 8);
+    im.off_part_o = off;   off = align256(off + size_t(slots) * hg * p.group_tile * L.head_dim * 4);
+    im.off_part_ml = off;  off = align256(off + size_t(slots) * hg * p.group_tile * 8);
     im.bytes = off;
     p.host_image.assign(im.off_part_o, 0);
     std::memcpy(p.host_image.data() + im.off_cta, p.cta_off.data(), p.cta_off.size() * 4);

@@ -18,7 +18,7 @@ pd_status fail(pd_status status, const std::string &msg);
 const std::string &last_error();
 
 struct DeviceImage {
-    size_t off_error = 0, off_cta = 0, off_segs = 0, off_groups = 0, off_counters = 0;
+    size_t off_error = 0, off_cta = 0, off_segs = 0, off_groups = 0;
     size_t off_table = 0, off_part_o = 0, off_part_ml = 0, bytes = 0;
 };
 
@@ -45,13 +45,14 @@ struct pd_plan {
     int32_t num_ctas = 0;
     int32_t splits = 1;
     int32_t max_context = 0;
-    int32_t num_pieces = 0;
+    int32_t num_pieces = 0;        // partial slots (segments that write partials x slot_stride)
+    int32_t slot_stride = 1;       // partial slots per segment: NC0 / HG sub-pipelines
     int64_t total_pages = 0;
     std::vector<int32_t> table;    // [B * W]
     std::vector<int32_t> lengths;  // [B]
     std::vector<int32_t> cta_off;  // [C + 1]
     std::vector<int32_t> segs;     // 4 per segment
-    std::vector<int32_t> groups;   // 8 per group: b, kv0, qoff, nh, length, piece0, npieces, 0
+    std::vector<int32_t> groups;   // 8 per group: b, kv0, qoff, nh, length, slot0 (-1: direct), segments, 0
     pd::DeviceImage image;
     std::vector<uint8_t> host_image;  // metadata part of the device buffer
     uint8_t *dev = nullptr;           // bound device buffer (caller-owned)

@@ -29,6 +29,7 @@ class PlanInfo(ctypes.Structure):
     _fields_ = [("splits", ctypes.c_int32), ("max_context", ctypes.c_int32),
                 ("num_ctas", ctypes.c_int32), ("num_segments", ctypes.c_int32),
                 ("num_groups", ctypes.c_int32), ("num_pieces", ctypes.c_int32),
+                ("slot_stride", ctypes.c_int32),
                 ("group_tile", ctypes.c_int32), ("heads_per_tile", ctypes.c_int32),
                 ("total_pages", ctypes.c_int32),
                 ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64)]

@@ -96,10 +96,10 @@ class DecodePlan:
     The output is borrowed storage, overwritten by the next run.  A plan may
     be used on one stream at a time; use distinct plans for concurrent streams.
 
-    ``merge`` is accepted for compatibility: the B200 kernel always merges
-    split partials inside the decode kernel (the last CTA of a group merges),
-    and ``merge_implementation`` keeps the reference's classification
-    ("serial", "shared" or "serial_fallback", runtime.py:54).
+    ``merge`` is accepted for compatibility: the B200 path always merges split
+    partials the same way (a merge kernel launched programmatically dependent
+    on the decode kernel), and ``merge_implementation`` keeps the reference's
+    classification ("serial", "shared" or "serial_fallback", runtime.py:54).
     ``num_ctas`` (extension) overrides the persistent grid size, which by
     default is one CTA per SM.
     """
@@ -157,6 +157,12 @@ class DecodePlan:
     @property
     def num_ctas(self):
         return int(self.info.num_ctas)
+
+    @property
+    def kernels_per_run(self):
+        """CUDA kernels one ``run`` launches: the decode kernel, plus the
+        dependent merge kernel when some (sequence, KV head) groups were split."""
+        return 1 + int(self.info.num_pieces > 0)
 
     def _check_inputs(self, q, k, v):
         import torch

@@ -45,29 +45,36 @@ def check_worklist(layout, table, lengths, plan):
     per_cta = [int((segs[offs[c]:offs[c + 1], 2] - segs[offs[c]:offs[c + 1], 1]).sum()) for c in range(C)]
     if total:
         assert min(per_cta) >= total // C and max(per_cta) <= -(-total // C)
+    stride = info["slot_stride"]
+    assert stride == max(1, (4 if gt == 32 else 8) // hg)
     covered = {gi: [] for gi in range(len(groups))}
     for c in range(C):
         for s in segs[offs[c]:offs[c + 1]]:
             covered[int(s[0])].append((int(s[1]), int(s[2]), int(s[3])))
-    used_pieces = []
+    slot_ranges = []
     for gi, ranges in covered.items():
         pages = -(-int(groups[gi][4]) // T)
         ranges.sort()
         assert ranges, f"group {gi} has no segment"
+        assert groups[gi][6] == len(ranges)
         if pages == 0:
-            assert ranges == [(0, 0, -1)]
-            continue
-        assert ranges[0][0] == 0 and ranges[-1][1] == pages
-        for (a0, a1, _), (b0, b1, _) in zip(ranges, ranges[1:]):
-            assert a1 == b0 and a0 < a1
-        pieces = [r[2] for r in ranges]
-        if len(ranges) == 1:
-            assert pieces == [-1] and groups[gi][5] == -1 and groups[gi][6] == 1
+            assert len(ranges) == 1 and ranges[0][:2] == (0, 0)
         else:
-            assert groups[gi][6] == len(ranges)
-            assert sorted(pieces) == list(range(groups[gi][5], groups[gi][5] + len(ranges)))
-            used_pieces += pieces
-    assert sorted(used_pieces) == list(range(info["num_pieces"]))
+            assert ranges[0][0] == 0 and ranges[-1][1] == pages
+            for (a0, a1, _), (b0, b1, _) in zip(ranges, ranges[1:]):
+                assert a1 == b0 and a0 < a1
+        slots = [r[2] for r in ranges]
+        if groups[gi][5] < 0:
+            # whole group on one CTA, one warp per head: direct output
+            assert len(ranges) == 1 and stride == 1 and slots == [-1]
+        else:
+            base = int(groups[gi][5])
+            assert sorted(slots) == [base + k * stride for k in range(len(ranges))]
+            slot_ranges.append((base, base + len(ranges) * stride))
+    slot_ranges.sort()
+    assert all(a[1] == b[0] for a, b in zip(slot_ranges, slot_ranges[1:]))
+    assert (slot_ranges[0][0] if slot_ranges else 0) == 0
+    assert (slot_ranges[-1][1] if slot_ranges else 0) == info["num_pieces"]
 
 
 @pytest.mark.parametrize("ctas", [1, 2, 3, 7, 64, 148, 1000])

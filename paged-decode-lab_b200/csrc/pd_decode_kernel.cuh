@@ -634,61 +634,85 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
 }
 
 // ------------------------------------------------------------------ partial merge
-// One warp per (group, KV head of the group, query head g): max-corrected merge
-// (oracle.py:88-96 algebra) of the partials written by `nsub` sub-pipelines
-// over each of the group's segments.  Launched programmatically dependent on
-// the decode kernel: griddepcontrol.wait returns once that grid has finished
-// and its writes are visible.
+// One CTA per output row (group, KV head hh of the group, query head g):
+// max-corrected merge (the oracle.py:88-96 algebra) of the partials that
+// `nsub` sub-pipelines wrote for each of the group's segments.  Warp 0 finds
+// the maximum M and denominator L; then each thread owns one float4 of head
+// dims and every R-th partial (R = 256 / (D/4)), and the R partial sums are
+// added in shared memory.  Launched programmatically dependent on the decode
+// kernel: griddepcontrol.wait returns once that grid has finished and its
+// writes are visible.
+constexpr int kMergeThreads = 256;
+
 template <int HG, int GT>
-__global__ void __launch_bounds__(128) merge_partials_kernel(const DecodeArgs a, int nsub, int D) {
+__global__ void __launch_bounds__(kMergeThreads) merge_partials_kernel(const DecodeArgs a, int nsub, int D) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int64_t wid = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = int64_t(a.num_groups) * HG * GT;
-    if (wid >= rows) return;
-    const int gi = int(wid / (HG * GT));
-    const int hh = int(wid / GT % HG);
-    const int g = int(wid % GT);
+    __shared__ float4 sums[kMergeThreads];
+    __shared__ float2 top_den;
+    const int64_t rowid = blockIdx.x;
+    const int gi = int(rowid / (HG * GT));
+    const int hh = int(rowid / GT % HG);
+    const int g = int(rowid % GT);
     const int4 g0 = a.groups[2 * gi];
     const int4 g1 = a.groups[2 * gi + 1];
     if (g1.y < 0 || g >= g0.w) return;         // written directly, or a padding head
     const int parts = g1.z * nsub;
-    auto slot_of = [&](int p) { return int64_t(g1.y) + int64_t(p / nsub) * a.slot_stride + p % nsub; };
-    float top = -INFINITY;
-    for (int p = lane; p < parts; p += 32) {
-        const float2 ml = a.part_ml[(slot_of(p) * HG + hh) * GT + g];
-        if (ml.y > 0.f) top = fmaxf(top, ml.x);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(kFullMask, top, o));
-    float den = 0.f;
-    for (int p = lane; p < parts; p += 32) {
-        const float2 ml = a.part_ml[(slot_of(p) * HG + hh) * GT + g];
-        if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(kFullMask, den, o);
-    const int64_t row = int64_t(g0.x) * a.Hq + int64_t(g0.y + hh) * a.group + g0.z + g;
-    for (int d0 = lane * 4; d0 < D; d0 += 128) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-        for (int p = 0; p < parts; ++p) {
-            const int64_t pr = slot_of(p) * HG + hh;
-            const float2 ml = a.part_ml[pr * GT + g];
-            if (ml.y > 0.f) {
-                const float w = exp2f(ml.x - top);
-                const float4 o = *reinterpret_cast<const float4 *>(a.part_o + (pr * GT + g) * D + d0);
-                acc.x = fmaf(w, o.x, acc.x);
-                acc.y = fmaf(w, o.y, acc.y);
-                acc.z = fmaf(w, o.z, acc.z);
-                acc.w = fmaf(w, o.w, acc.w);
-            }
+    auto slot_row = [&](int p) {
+        return (int64_t(g1.y) + int64_t(p / nsub) * a.slot_stride + p % nsub) * HG + hh;
+    };
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < 32) {
+        float top = -INFINITY;
+        for (int p = lane; p < parts; p += 32) {
+            const float2 ml = a.part_ml[slot_row(p) * GT + g];
+            if (ml.y > 0.f) top = fmaxf(top, ml.x);
         }
-        *reinterpret_cast<float4 *>(a.out + row * D + d0) =
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(kFullMask, top, o));
+        float den = 0.f;
+        for (int p = lane; p < parts; p += 32) {
+            const float2 ml = a.part_ml[slot_row(p) * GT + g];
+            if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(kFullMask, den, o);
+        if (lane == 0) top_den = make_float2(top, den);
+    }
+    __syncthreads();
+    const float top = top_den.x, den = top_den.y;
+    const int chunks = D / 4;                   // float4 chunks per row
+    const int lanes_p = kMergeThreads / chunks; // partials summed in parallel
+    const int c = tid % chunks, r = tid / chunks;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int p = r; p < parts; p += lanes_p) {
+        const int64_t pr = slot_row(p);
+        const float2 ml = a.part_ml[pr * GT + g];
+        if (ml.y > 0.f) {
+            const float w = exp2f(ml.x - top);
+            const float4 o = reinterpret_cast<const float4 *>(a.part_o + (pr * GT + g) * D)[c];
+            acc.x = fmaf(w, o.x, acc.x);
+            acc.y = fmaf(w, o.y, acc.y);
+            acc.z = fmaf(w, o.z, acc.z);
+            acc.w = fmaf(w, o.w, acc.w);
+        }
+    }
+    sums[tid] = acc;
+    __syncthreads();
+    if (r == 0) {
+        for (int k = 1; k < lanes_p; ++k) {
+            const float4 v = sums[k * chunks + c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int64_t row = int64_t(g0.x) * a.Hq + int64_t(g0.y + hh) * a.group + g0.z + g;
+        reinterpret_cast<float4 *>(a.out + row * D)[c] =
             den > 0.f ? make_float4(acc.x / den, acc.y / den, acc.z / den, acc.w / den)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.stats && c == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
     }
-    if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
 }
 
 }  // namespace pd

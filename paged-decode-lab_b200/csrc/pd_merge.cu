@@ -36,10 +36,11 @@ static __global__ void merge_shards_kernel(const float *__restrict__ shard_out,
 
 template <int HG, int GT>
 static cudaError_t launch_merge(const DecodeArgs &args, int nsub, int D, cudaStream_t stream) {
-    const int64_t warps = int64_t(args.num_groups) * HG * GT;
+    const int64_t rows = int64_t(args.num_groups) * HG * GT;
+    if (rows > INT32_MAX) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned((warps + 3) / 4));
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3(unsigned(rows));
+    cfg.blockDim = dim3(kMergeThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

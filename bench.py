@@ -75,52 +75,67 @@ def measured_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled while the timed region runs.
 
-    def __init__(self, device_index):
+    NVML (the library nvidia-smi reads) is polled every millisecond from a
+    background thread, so even a few-millisecond timed region gets samples;
+    falls back to `nvidia-smi -lms 200` when NVML is unavailable.
+    """
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
+
+    def __init__(self, device_index, period_s=0.001):
         self.device_index = device_index
-        self.proc = None
+        self.period_s = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - NVML missing: no samples, reported as such
+            return self
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                    reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    self.samples.append((mhz, reasons))
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(self.period_s)
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
+    def _physical_index(self):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if visible:
+            ids = [x for x in visible.split(",") if x.strip()]
+            if self.device_index < len(ids) and ids[self.device_index].strip().isdigit():
+                return int(ids[self.device_index])
+        return self.device_index
+
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
         return False
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f == "Active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        reasons = sorted(name for name, bit in self.REASONS.items()
+                         if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
 
 
 def algorithmic_bytes(w):
@@ -307,13 +322,14 @@ def run_ours(args, rank, local, world):
                                 f"kv_head, weak: rank r owns KV heads [8r, 8r+8) of a {8 * world}-KV-head "
                                 "model, same sequences on every rank, no collective"),
                    "l2": ("inputs larger than L2" if flush is None else "L2 flushed between steps"),
-                   "persistent_ctas": plan.num_ctas},
+                   "persistent_ctas": plan.num_ctas,
+                   "kv_heads_per_tile": int(plan.native_info(q.dtype).heads_per_tile)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic, "kernel": "paged_decode_kernel",
                      "kernel_us": kernel_ms * 1e3,
                      "algorithmic_bytes_per_launch": nbytes},
-        "gpu_launches": args.steps * plan.kernels_per_run,
+        "gpu_launches": args.steps * plan.kernels_per_run(q.dtype),
         "clocks": clocks.summary(),
     }
     if e2e:

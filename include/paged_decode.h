@@ -84,12 +84,15 @@ typedef struct pd_plan_info {
  * (decode.cu:201-237).  Copies table and lengths.  merge_mode 0 = "serial",
  * 1 = "shared" is accepted for API compatibility (runtime.py:33-34); the
  * decode always merges split partials the same way (a dependent merge kernel
- * launched right behind the decode kernel).  device < 0 builds a host-only plan
- * (inspection, no decode).  num_ctas <= 0 picks one CTA per SM of device.
+ * launched right behind the decode kernel).  A plan serves one input dtype:
+ * the page tiles it gathers are sized for it (the Python DecodePlan keeps one
+ * plan per dtype behind its dtype-agnostic run()).  device < 0 builds a
+ * host-only plan (inspection, no decode).  num_ctas <= 0 picks one CTA per SM
+ * of device.
  */
 pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
                          const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                         int32_t device, int32_t num_ctas, pd_plan **out_plan);
+                         pd_dtype dtype, int32_t device, int32_t num_ctas, pd_plan **out_plan);
 
 void pd_plan_destroy(pd_plan *plan);
 
@@ -118,8 +121,9 @@ pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *s
 
 /* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
  * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
- * k and v must be 16-byte aligned (TMA).  Asynchronous on `stream`: one
- * decode kernel, plus a merge kernel when the plan has partial slots.
+ * k and v must be 16-byte aligned (TMA); dtype must be the plan's.
+ * Asynchronous on `stream`: one decode kernel, plus a merge kernel when the
+ * plan has partial slots.
  */
 pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
                     float *out, void *stream);

@@ -105,9 +105,10 @@ pd_status check_bound(const pd_plan *p) {
     return PD_OK;
 }
 
-pd_status check_dtype(pd_dtype dtype) {
+pd_status check_dtype(const pd_plan *p, pd_dtype dtype) {
     if (dtype != PD_FLOAT16 && dtype != PD_FLOAT32)
         return fail(PD_ERR_TYPE, "q/k/v must share float16 or float32 dtype");
+    if (dtype != p->dtype) return fail(PD_ERR_TYPE, "input dtype differs from the plan's dtype");
     return PD_OK;
 }
 
@@ -173,7 +174,7 @@ pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, p
                       float *out, float *stats, void *stream) {
     pd_status s = check_bound(p);
     if (s != PD_OK) return s;
-    if ((s = check_dtype(dtype)) != PD_OK) return s;
+    if ((s = check_dtype(p, dtype)) != PD_OK) return s;
     if (!q || !out) return fail(PD_ERR_VALUE, "q and out must not be NULL");
     if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
         return fail(PD_ERR_VALUE, "q and out must be 16-byte aligned");
@@ -193,7 +194,7 @@ using namespace pd;
 
 PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
                                 const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                                int32_t device, int32_t num_ctas, pd_plan **out_plan) {
+                                pd_dtype dtype, int32_t device, int32_t num_ctas, pd_plan **out_plan) {
     if (!out_plan) return fail(PD_ERR_VALUE, "out_plan must not be NULL");
     *out_plan = nullptr;
     int sm_count = 148;
@@ -205,7 +206,7 @@ PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, i
     pd_plan *p = new (std::nothrow) pd_plan();
     if (!p) return fail(PD_ERR_VALUE, "out of host memory");
     const pd_status s =
-        build_plan(layout, table, table_width, lengths, split_tokens, merge_mode, num_ctas, sm_count, *p);
+        build_plan(layout, table, table_width, lengths, split_tokens, merge_mode, dtype, num_ctas, sm_count, *p);
     if (s != PD_OK) {
         delete p;
         return s;
@@ -295,7 +296,7 @@ PD_API pd_status pd_gather_debug(pd_plan *p, const void *k, const void *v, pd_dt
                                  void *dense_k, void *dense_v, void *stream) {
     pd_status s = check_bound(p);
     if (s != PD_OK) return s;
-    if ((s = check_dtype(dtype)) != PD_OK) return s;
+    if ((s = check_dtype(p, dtype)) != PD_OK) return s;
     if (!dense_k || !dense_v) return fail(PD_ERR_VALUE, "dense outputs must not be NULL");
     if ((reinterpret_cast<uintptr_t>(dense_k) | reinterpret_cast<uintptr_t>(dense_v)) & 15)
         return fail(PD_ERR_VALUE, "dense outputs must be 16-byte aligned");

@@ -5,11 +5,11 @@ namespace pd {
 
 // Largest KV-head group (1, 2, 4 or 8; at most the consumer warps per CTA,
 // which is 4 when 32 query heads share a KV head and 8 otherwise; dividing
-// kv_heads) whose FP16 page tile (K + V) stays within `target_bytes`, which
-// is capped at the 64 KiB the kernels are instantiated for.
-inline int choose_heads_per_tile(int D, int T, int GT, int kv_heads, int target_bytes) {
+// kv_heads) whose page tile (K + V of elt-byte elements) stays within
+// `target_bytes`, which is capped at 64 KiB.
+inline int choose_heads_per_tile(int elt, int D, int T, int GT, int kv_heads, int target_bytes) {
     const int nc0 = GT == 32 ? 4 : 8;
-    const int per_head = 2 * D * 2 * T;
+    const int per_head = 2 * D * elt * T;
     if (target_bytes > 65536) target_bytes = 65536;
     int best = 1;
     for (int hg = 2; hg <= nc0; hg *= 2)

@@ -23,9 +23,10 @@ namespace pd {
 
 namespace {
 thread_local std::string g_last_error;
-// FP16 page tiles (K + V of HG heads) aim at this size: four TMA boxes of
-// 8 KiB each keep the single issuing thread far ahead of HBM.
-constexpr int kTileTargetBytes = 32 * 1024;
+// Page tiles (K + V of HG heads) aim at this size: four TMA boxes of up to
+// 16 KiB each keep the single issuing thread far ahead of HBM (a TMA
+// instruction costs about the same to issue whatever its size).
+constexpr int kTileTargetBytes = 64 * 1024;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
@@ -41,7 +42,7 @@ const std::string &last_error() { return g_last_error; }
 
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
                      const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                     int32_t num_ctas, int32_t sm_count, pd_plan &p) {
+                     pd_dtype dtype, int32_t num_ctas, int32_t sm_count, pd_plan &p) {
     if (!layout) return fail(PD_ERR_VALUE, "layout must not be NULL");
     const pd_layout L = *layout;
     // Layout.__post_init__ (oracle.py:24-27)
@@ -61,6 +62,8 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         return fail(PD_ERR_VALUE, "batch/head count exceeds CUDA grid limits");
     if (split_tokens < 1 || split_tokens > 1048576)
         return fail(PD_ERR_VALUE, "split_tokens must be an integer in [1,1048576]");
+    if (dtype != PD_FLOAT16 && dtype != PD_FLOAT32)
+        return fail(PD_ERR_TYPE, "q/k/v must share float16 or float32 dtype");
     // validate_metadata (oracle.py:30-47)
     if (width < 0) return fail(PD_ERR_VALUE, "page table must have shape [batch, logical_pages]");
     if (!lengths || (width > 0 && !table))
@@ -94,6 +97,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     p.width = width;
     p.split_tokens = split_tokens;
     p.merge_mode = merge_mode;
+    p.dtype = dtype;
     p.splits = int32_t(splits);
     p.max_context = max_context;
     p.group = L.query_heads / L.kv_heads;
@@ -109,13 +113,14 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // A group is (sequence b, KV-head group of HG heads, query-head tile gs):
     // its page tiles carry HG heads' K and V for one page.
     const int T = L.page_size;
-    // PD_TILE_KIB overrides the FP16 tile target (tuning; capped at 64 KiB).
+    // PD_TILE_KIB overrides the tile target (tuning; capped at 64 KiB).
     int target = kTileTargetBytes;
     if (const char *env = std::getenv("PD_TILE_KIB")) {
         const int kib = std::atoi(env);
         if (kib >= 1) target = kib * 1024;
     }
-    const int hg = choose_heads_per_tile(L.head_dim, T, p.group_tile, L.kv_heads, target);
+    const int hg = choose_heads_per_tile(dtype == PD_FLOAT16 ? 2 : 4, L.head_dim, T, p.group_tile,
+                                         L.kv_heads, target);
     p.heads_per_tile = hg;
     const int kv_groups = L.kv_heads / hg;
     const int64_t ngroups = int64_t(L.batch) * kv_groups * p.group_splits;

@@ -38,6 +38,7 @@ struct pd_plan {
     int32_t split_tokens = 0;
     int32_t merge_mode = 0;
     int32_t device = -1;
+    pd_dtype dtype = PD_FLOAT16;
     int32_t group = 0;             // G = Hq / Hkv
     int32_t group_tile = 8;        // GT: query heads processed together (8, 16, 32)
     int32_t group_splits = 1;      // ceil(G / GT)
@@ -66,6 +67,6 @@ namespace pd {
 // num_ctas <= 0.  Mirrors the checks of runtime.py:33-51 and oracle.py:20-47.
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
                      const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                     int32_t num_ctas, int32_t sm_count, pd_plan &plan);
+                     pd_dtype dtype, int32_t num_ctas, int32_t sm_count, pd_plan &plan);
 
 }  // namespace pd

@@ -37,7 +37,7 @@ class PlanInfo(ctypes.Structure):
 
 SIGNATURES = {
     "pd_plan_create": (_c_int32, [ctypes.POINTER(Layout), _vp, _c_int64, _vp, _c_int32, _c_int32,
-                                  _c_int32, _c_int32, ctypes.POINTER(_vp)]),
+                                  _c_int32, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
     "pd_plan_destroy": (None, [_vp]),
     "pd_plan_get_info": (_c_int32, [_vp, ctypes.POINTER(PlanInfo)]),
     "pd_plan_copy_worklist": (_c_int32, [_vp, _vp, _vp, _vp]),

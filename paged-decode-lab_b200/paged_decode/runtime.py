@@ -43,7 +43,7 @@ def _check_limits(layout, split_tokens, merge):
         raise ValueError("split_tokens must be an integer in [1,1048576]")
 
 
-def _native_plan(layout, table, lengths, split_tokens, merge, device_index, num_ctas):
+def _native_plan(layout, table, lengths, split_tokens, merge, dtype_code, device_index, num_ctas):
     lib = _native.load()
     c_layout = _native.Layout(layout.batch, layout.query_heads, layout.kv_heads, layout.head_dim,
                               layout.page_size, layout.physical_pages)
@@ -52,7 +52,7 @@ def _native_plan(layout, table, lengths, split_tokens, merge, device_index, num_
     handle = ctypes.c_void_p()
     _native.check(lib.pd_plan_create(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
                                      lengths.ctypes.data, split_tokens, int(merge == "shared"),
-                                     device_index, num_ctas or 0, ctypes.byref(handle)),
+                                     dtype_code, device_index, num_ctas or 0, ctypes.byref(handle)),
                   "plan")
     return handle
 
@@ -68,24 +68,50 @@ def _worklist(lib, handle):
     return info, segs, groups, offsets
 
 
-def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=148):
-    """Build a host-only plan (no GPU needed) and return its work list.
+_DTYPE_CODES = {"float16": _native.PD_FLOAT16, "float32": _native.PD_FLOAT32}
+
+
+def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=148, dtype="float16"):
+    """Build a host-only plan (no GPU needed) for one input dtype and return its work list.
 
     Returns a dict with ``info`` (pd_plan_info fields), ``segments``
-    [n, 4] = (group, first_page, end_page, piece), ``groups`` [g, 8] =
-    (batch, kv_head, first_query_head, query_heads, length, first_piece,
-    pieces, 0) and ``cta_offsets`` [num_ctas + 1].
+    [n, 4] = (group, first_page, end_page, first partial slot or -1),
+    ``groups`` [g, 8] = (batch, first_kv_head, query_head_offset, query_heads,
+    length, first partial slot or -1, segments, 0) and ``cta_offsets``
+    [num_ctas + 1].
     """
     _check_limits(layout, split_tokens, "serial")
     table, lengths = validate_metadata(layout, table, lengths)
     lib = _native.load()
-    handle = _native_plan(layout, table, lengths, split_tokens, "serial", -1, num_ctas)
+    handle = _native_plan(layout, table, lengths, split_tokens, "serial", _DTYPE_CODES[dtype], -1, num_ctas)
     try:
         info, segs, groups, offsets = _worklist(lib, handle)
     finally:
         lib.pd_plan_destroy(handle)
     return {"info": {name: getattr(info, name) for name, _ in info._fields_},
             "segments": segs, "groups": groups, "cta_offsets": offsets}
+
+
+class _NativePlan:
+    """One C-ABI plan (one input dtype) and the device buffer it is bound to."""
+
+    def __init__(self, lib, layout, table, lengths, split_tokens, merge, dtype_code, device, num_ctas):
+        import torch
+        self._lib = lib
+        self.handle = _native_plan(layout, table, lengths, split_tokens, merge, dtype_code,
+                                   device.index, num_ctas)
+        self.info, self.segments, self.groups, self.cta_offsets = _worklist(lib, self.handle)
+        nbytes = int(lib.pd_plan_device_bytes(self.handle))
+        self.buffer = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _native.check(lib.pd_plan_bind(self.handle, self.buffer.data_ptr(), self.buffer.numel(), stream),
+                      "bind")
+
+    def __del__(self):
+        handle = getattr(self, "handle", None)
+        if handle:
+            self._lib.pd_plan_destroy(handle)
+            self.handle = None
 
 
 class DecodePlan:
@@ -128,41 +154,37 @@ class DecodePlan:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self._table_cpu, self._lengths_cpu = table, lengths
         self._lib = _native.load()
-        self._handle = _native_plan(layout, table, lengths, split_tokens, merge,
-                                    self.device.index, num_ctas)
-        self.info, self._segments, self._groups, self._cta_offsets = _worklist(self._lib, self._handle)
-        nbytes = int(self._lib.pd_plan_device_bytes(self._handle))
-        self._buffer = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        # one native plan per input dtype (page tiles are sized per dtype)
+        self._native = {code: _NativePlan(self._lib, layout, table, lengths, split_tokens, merge, code,
+                                          self.device, num_ctas)
+                        for code in (_native.PD_FLOAT16, _native.PD_FLOAT32)}
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
                                 dtype=torch.float32, device=self.device)
-        self._bind()
 
-    def _bind(self):
+    @property
+    def info(self):
+        """pd_plan_info of the FP16 plan (see ``native_info`` for FP32)."""
+        return self._native[_native.PD_FLOAT16].info
+
+    def native_info(self, dtype):
         import torch
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        _native.check(self._lib.pd_plan_bind(self._handle, self._buffer.data_ptr(),
-                                             self._buffer.numel(), stream), "bind")
-
-    def __del__(self):
-        handle = getattr(self, "_handle", None)
-        if handle:
-            self._lib.pd_plan_destroy(handle)
-            self._handle = None
+        return self._native[_native.PD_FLOAT16 if dtype == torch.float16 else _native.PD_FLOAT32].info
 
     @property
     def workspace_bytes(self):
-        """Split-K partial outputs, their (m, l) pairs and the merge counters."""
-        return int(self.info.workspace_bytes)
+        """Split-K partial outputs and their (m, l) pairs, over both dtype plans."""
+        return sum(int(n.info.workspace_bytes) for n in self._native.values())
 
     @property
     def num_ctas(self):
         return int(self.info.num_ctas)
 
-    @property
-    def kernels_per_run(self):
-        """CUDA kernels one ``run`` launches: the decode kernel, plus the
-        dependent merge kernel when some (sequence, KV head) groups were split."""
-        return 1 + int(self.info.num_pieces > 0)
+    def kernels_per_run(self, dtype=None):
+        """CUDA kernels one ``run`` launches: the decode kernel, plus the dependent
+        merge kernel when some (sequence, KV-head group) was split or sub-pipelined."""
+        import torch
+        info = self.native_info(dtype if dtype is not None else torch.float16)
+        return 1 + int(info.num_pieces > 0)
 
     def _check_inputs(self, q, k, v):
         import torch
@@ -185,8 +207,8 @@ class DecodePlan:
         import torch
         dtype = self._check_inputs(q, k, v)
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        _native.check(self._lib.pd_decode(self._handle, q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                          dtype, self._out.data_ptr(), stream), "decode")
+        _native.check(self._lib.pd_decode(self._native[dtype].handle, q.data_ptr(), k.data_ptr(),
+                                          v.data_ptr(), dtype, self._out.data_ptr(), stream), "decode")
         return self._out
 
     def run_with_stats(self, q, k, v, out, stats):
@@ -206,7 +228,7 @@ class DecodePlan:
                 raise ValueError("out/stats must be contiguous FP32 [B,Hq,D] / [B,Hq,2] on the plan device")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _native.check(self._lib.pd_decode_with_stats(
-            self._handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), dtype, out.data_ptr(),
+            self._native[dtype].handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), dtype, out.data_ptr(),
             stats.data_ptr(), stream), "decode")
         return out, stats
 
@@ -225,22 +247,27 @@ class DecodePlan:
         dense_k = torch.zeros(shape, dtype=k.dtype, device=self.device)
         dense_v = torch.zeros(shape, dtype=k.dtype, device=self.device)
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        _native.check(self._lib.pd_gather_debug(self._handle, k.data_ptr(), v.data_ptr(), dtype,
-                                                dense_k.data_ptr(), dense_v.data_ptr(), stream),
+        _native.check(self._lib.pd_gather_debug(self._native[dtype].handle, k.data_ptr(), v.data_ptr(),
+                                                dtype, dense_k.data_ptr(), dense_v.data_ptr(), stream),
                       "gather")
         return dense_k, dense_v
 
     def read_errors(self):
-        """Return and clear the device error word (synchronises the current stream)."""
+        """Return and clear the device error words (synchronises the current stream)."""
         import torch
-        word = ctypes.c_uint32(0)
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        _native.check(self._lib.pd_plan_read_errors(self._handle, ctypes.byref(word), stream))
-        return int(word.value)
+        total = 0
+        for plan in self._native.values():
+            word = ctypes.c_uint32(0)
+            _native.check(self._lib.pd_plan_read_errors(plan.handle, ctypes.byref(word), stream))
+            total |= int(word.value)
+        return total
 
-    def worklist(self):
-        """(segments, groups, cta_offsets) as NumPy arrays (see ``inspect_plan``)."""
-        return self._segments.copy(), self._groups.copy(), self._cta_offsets.copy()
+    def worklist(self, dtype=None):
+        """(segments, groups, cta_offsets) of the FP16 (or given dtype's) plan, see ``inspect_plan``."""
+        import torch
+        plan = self._native[_native.PD_FLOAT32 if dtype == torch.float32 else _native.PD_FLOAT16]
+        return plan.segments.copy(), plan.groups.copy(), plan.cta_offsets.copy()
 
     def split_bounds(self, b):
         """The reference's context partitions of sequence b: range(0, max(len,1), split_tokens)."""

@@ -52,7 +52,7 @@ def _create(layout, table, lengths, split=256, merge=0, device=-1, ctas=4):
     lengths = np.ascontiguousarray(lengths, dtype=np.int32)
     handle = ctypes.c_void_p()
     status = lib.pd_plan_create(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
-                                lengths.ctypes.data, split, merge, device, ctas, ctypes.byref(handle))
+                                lengths.ctypes.data, split, merge, 0, device, ctas, ctypes.byref(handle))
     return status, handle
 
 
@@ -89,7 +89,7 @@ def test_host_only_plan_cannot_bind_or_launch():
 
 def test_null_arguments_are_errors_not_crashes():
     lib = _native.load()
-    assert lib.pd_plan_create(None, None, 0, None, 256, 0, -1, 1, None) == _native.PD_ERR_VALUE
+    assert lib.pd_plan_create(None, None, 0, None, 256, 0, 0, -1, 1, None) == _native.PD_ERR_VALUE
     assert lib.pd_plan_get_info(None, None) == _native.PD_ERR_VALUE
     assert lib.pd_decode(None, None, None, None, 0, None, None) == _native.PD_ERR_VALUE
     assert lib.pd_merge_shards(None, None, 1, 1, 128, None, None) == _native.PD_ERR_VALUE

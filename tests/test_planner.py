@@ -28,8 +28,8 @@ def check_worklist(layout, table, lengths, plan):
     assert gt == (8 if G <= 8 else 16 if G <= 16 else 32)
     hg = info["heads_per_tile"]
     assert hg in (1, 2, 4, 8) and layout.kv_heads % hg == 0 and hg <= (4 if gt == 32 else 8)
-    # FP16 page tile (K + V of hg heads) within the 32 KiB target unless hg == 1
-    assert hg == 1 or hg * 2 * layout.head_dim * 2 * T <= 32 * 1024
+    # FP16 page tile (K + V of hg heads) within the 64 KiB target unless hg == 1
+    assert hg == 1 or hg * 2 * layout.head_dim * 2 * T <= 64 * 1024
     splits = math.ceil(G / gt)
     kv_groups = layout.kv_heads // hg
     assert info["num_groups"] == layout.batch * kv_groups * splits
@@ -128,9 +128,12 @@ def test_plan_errors_mirror_reference_messages():
         inspect_plan(layout, [[0.0, 1.0]], [17])
 
 
-@pytest.mark.parametrize("dim,page,kv_heads,expected", [
-    (128, 16, 8, 4), (128, 32, 8, 2), (64, 16, 8, 8), (64, 32, 32, 4), (128, 32, 1, 1), (128, 16, 6, 2)])
-def test_heads_per_tile_targets_32kib_fp16_tiles(dim, page, kv_heads, expected):
+@pytest.mark.parametrize("dim,page,kv_heads,dtype,expected", [
+    (128, 16, 8, "float16", 8), (128, 32, 8, "float16", 4), (64, 16, 8, "float16", 8),
+    (64, 32, 32, "float16", 8), (128, 32, 1, "float16", 1), (128, 16, 6, "float16", 2),
+    (128, 16, 8, "float32", 4), (64, 32, 32, "float32", 4), (128, 32, 8, "float32", 2)])
+def test_heads_per_tile_targets_64kib_tiles(dim, page, kv_heads, dtype, expected):
     layout = Layout(2, kv_heads * 4, kv_heads, dim, page, 8)
-    plan = inspect_plan(layout, np.arange(8, dtype=np.int32).reshape(2, 4), [page * 4, 1], num_ctas=3)
+    plan = inspect_plan(layout, np.arange(8, dtype=np.int32).reshape(2, 4), [page * 4, 1], num_ctas=3,
+                        dtype=dtype)
     assert plan["info"]["heads_per_tile"] == expected

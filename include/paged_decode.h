@@ -154,6 +154,28 @@ pd_status pd_merge_shards(const float *shard_out, const float *shard_stats, int3
 pd_status pd_gather_debug(pd_plan *plan, const void *k, const void *v, pd_dtype dtype,
                           void *dense_k, void *dense_v, void *stream);
 
+/* As pd_decode, but with no device memory from the caller or the library.
+ * No counterpart in the reference: it exists for callers that cannot call
+ * cudaMalloc (their device memory is owned by another framework's pool, or
+ * they may only touch the buffers they are handed).  The plan needs no
+ * pd_plan_bind; its metadata and split-K partials go to one file-scope
+ * device array of pd_static_scratch_capacity() bytes (16 MiB) that every
+ * GPU loading this library holds until exit.  A plan needing more
+ * (pd_plan_device_bytes) is rejected with PD_ERR_VALUE.  Each call uploads
+ * the plan's metadata into the array on `stream` (overwriting the previous
+ * call's contents and zeroing its error word), then launches.  All calls
+ * share the array: calls that overlap on the GPU (other streams, devices'
+ * own arrays aside) race.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  Allocates nothing: no cudaMalloc,
+ * cudaFree or allocating library routine.
+ */
+pd_status pd_decode_static(pd_plan *plan, const void *q, const void *k, const void *v,
+                           pd_dtype dtype, float *out, void *stream);
+
+/* Size of the device array pd_decode_static uses (bytes). */
+size_t pd_static_scratch_capacity(void);
+
 /* Copy the device error word to *error_word and clear it (synchronises `stream`). */
 pd_status pd_plan_read_errors(pd_plan *plan, uint32_t *error_word, void *stream);
 

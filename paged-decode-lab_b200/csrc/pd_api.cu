@@ -112,9 +112,8 @@ pd_status check_dtype(const pd_plan *p, pd_dtype dtype) {
     return PD_OK;
 }
 
-DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
+DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, float *stats) {
     DecodeArgs a{};
-    uint8_t *dev = p->dev;
     const DeviceImage &im = p->image;
     a.q = q;
     a.table = reinterpret_cast<const int32_t *>(dev + im.off_table);
@@ -136,6 +135,10 @@ DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
+}
+
+DecodeArgs make_args(pd_plan *p, const void *q, float *out, float *stats) {
+    return make_args_at(p, p->dev, q, out, stats);
 }
 
 pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int mode,
@@ -290,6 +293,74 @@ PD_API pd_status pd_merge_shards(const float *shard_out, const float *shard_stat
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
     return PD_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Decode without any device allocation by the caller or the library.
+//
+// Callers that cannot call cudaMalloc (a host program whose device memory is
+// owned and pooled by another framework, a plugin that may only touch the
+// buffers it is handed, code running where allocation is forbidden) still
+// need somewhere to put a plan's metadata and split-K partials.  This entry
+// point uses one file-scope device array instead: every GPU that loads this
+// library holds it (kStaticScratchBytes) until the process exits.
+namespace pd {
+namespace {
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;
+__device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mutex;
+constexpr int kMaxDevices = 256;
+uint8_t *g_static_address[kMaxDevices] = {};
+
+// The symbol names a host-side stand-in; the device address must come from
+// cudaGetSymbolAddress, taken once per device with that device current.
+pd_status static_scratch(int device, uint8_t **out) {
+    if (device < 0 || device >= kMaxDevices) return fail(PD_ERR_VALUE, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_address[device]) {
+        void *ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (err != cudaSuccess || !ptr)
+            return fail(PD_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err));
+        g_static_address[device] = static_cast<uint8_t *>(ptr);
+    }
+    *out = g_static_address[device];
+    return PD_OK;
+}
+}  // namespace
+}  // namespace pd
+
+PD_API size_t pd_static_scratch_capacity(void) { return kStaticScratchBytes; }
+
+PD_API pd_status pd_decode_static(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
+                                  float *out, void *stream) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (p->device < 0) return fail(PD_ERR_VALUE, "host-only plan (device < 0) cannot launch");
+    pd_status s = check_dtype(p, dtype);
+    if (s != PD_OK) return s;
+    if (!q || !out) return fail(PD_ERR_VALUE, "q and out must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return fail(PD_ERR_VALUE, "q and out must be 16-byte aligned");
+    if (p->image.bytes > kStaticScratchBytes)
+        return fail(PD_ERR_VALUE, "plan needs " + std::to_string(p->image.bytes) +
+                                      " bytes of scratch; pd_decode_static has " +
+                                      std::to_string(kStaticScratchBytes));
+    DeviceGuard guard(p->device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    uint8_t *scratch = nullptr;
+    if ((s = static_scratch(p->device, &scratch)) != PD_OK) return s;
+    // This call's metadata (and a zeroed error word) replace whatever the last
+    // call left in the shared array; partial slots are always written before
+    // they are read, so they need no clearing.
+    const auto st = static_cast<cudaStream_t>(stream);
+    const cudaError_t err =
+        cudaMemcpyAsync(scratch, p->host_image.data(), p->host_image.size(), cudaMemcpyHostToDevice, st);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("scratch upload: ") + cudaGetErrorString(err));
+    const DecodeArgs args = make_args_at(p, scratch, q, out, nullptr);
+    return launch(p, k, v, dtype, kModeDecode, args, stream);
 }
 
 PD_API pd_status pd_gather_debug(pd_plan *p, const void *k, const void *v, pd_dtype dtype,

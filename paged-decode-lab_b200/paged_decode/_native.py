@@ -48,6 +48,8 @@ SIGNATURES = {
     "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_plan_read_errors": (_c_int32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "pd_decode_static": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
+    "pd_static_scratch_capacity": (_c_size, []),
     "pd_status_string": (ctypes.c_char_p, [_c_int32]),
     "pd_last_error": (ctypes.c_char_p, []),
     "pd_abi_version": (_c_int32, []),

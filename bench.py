@@ -9,11 +9,14 @@ sequence is read once per KV head.  Default workload
 (B32 ragged lengths 0..8192 with a shared 64-page prefix, 32:8 heads, D128,
 FP16, page 16, split 256), seeded synthetic data.
 
-N > 1 (torchrun, one rank per GPU, NCCL): KV-head sharding with weak scaling.
-Every rank serves the same sequences (same page tables and lengths) for its
-own 8 KV heads and their 32 query heads, i.e. rank r owns KV heads
-[8r, 8r+8) of an 8N-KV-head model; there is no data-path collective.
-value = all ranks' algorithmic bytes / max-over-ranks step time.
+N > 1 (torchrun, one rank per GPU, NCCL): by default KV-head sharding with
+weak scaling.  Every rank serves the same sequences (same page tables and
+lengths) for its own 8 KV heads and their 32 query heads, i.e. rank r owns KV
+heads [8r, 8r+8) of an 8N-KV-head model; there is no data-path collective.
+--scaling strong splits the chosen config itself: KV heads across ranks, or
+(c5, --sharding sequence) contiguous page runs of every sequence with an NCCL
+all-gather of (o, m, l) and a merge.  value = all ranks' algorithmic bytes /
+max-over-ranks step time.
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier +
 synchronize, device time from CUDA events on the launching stream; each step
@@ -59,6 +62,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3a", "c3b", "c3c", "c4", "c5"])
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N > 1: weak = KV-head shards of an N x larger model; strong = split this config")
+    ap.add_argument("--sharding", choices=["kv_head", "sequence"], default=None,
+                    help="strong scaling split (default: sequence for c5, kv_head otherwise)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -212,25 +219,94 @@ def cpu_baseline(w, q, k, v, nbytes, budget_s, steps=None):
 
 
 # ---------------------------------------------------------------------- our implementation
-def run_ours(args, rank, local, world):
-    import numpy as np
-    import torch
-    from paged_decode import workload
-    from paged_decode.runtime import DecodePlan
+class RankJob:
+    """What one rank decodes per step, and how the job's bytes are counted."""
 
-    w = workload.CONFIGS[args.workload]()
-    w.seed = w.seed + rank          # rank r: its own KV heads' data, same sequences
-    q, k, v = w.tensors("cuda")
-    plan = DecodePlan(w.layout, w.table, w.lengths, split_tokens=w.split_tokens)
-    nbytes = algorithmic_bytes(w)
+    def __init__(self, args, rank, world):
+        import torch
+        from paged_decode import dist as pd_dist
+        from paged_decode import workload
+        from paged_decode.layout import Layout
+
+        w = workload.CONFIGS[args.workload]()
+        self.workload = w
+        L = w.layout
+        self.sharding = "none"
+        self.bytes_total = algorithmic_bytes(w)
+        self.extra_kernels = 0
+        if world == 1:
+            from paged_decode.runtime import DecodePlan
+            self.plan = DecodePlan(L, w.table, w.lengths, split_tokens=w.split_tokens)
+            self.q, self.k, self.v = w.tensors("cuda")
+            self.run = lambda q: self.plan.run(q, self.k, self.v)
+            self.decode_plan = self.plan
+            self.bytes_rank = self.bytes_total
+            return
+        mode = args.sharding or ("sequence" if args.workload == "c5" else "kv_head")
+        if args.scaling == "weak":
+            # KV-head sharding of a model with world x the config's KV heads: every rank
+            # serves the same sequences for its own heads (same local geometry as config).
+            glob = Layout(L.batch, L.query_heads * world, L.kv_heads * world, L.head_dim, L.page_size,
+                          L.physical_pages)
+            plan = pd_dist.KVHeadShardedPlan(glob, w.table, w.lengths, rank=rank, world=world,
+                                             split_tokens=w.split_tokens)
+            w.seed += rank
+            self.q, self.k, self.v = w.tensors("cuda")
+            self.run = lambda q: plan.run(q, self.k, self.v)
+            self.decode_plan = plan.plan
+            self.bytes_rank = self.bytes_total
+            self.bytes_total *= world
+            self.sharding = (f"kv_head, weak: rank r owns KV heads [{L.kv_heads}r, {L.kv_heads}r+{L.kv_heads}) "
+                             f"of a {L.kv_heads * world}-KV-head model; same sequences on every rank; "
+                             "no collective")
+        elif mode == "kv_head":
+            plan = pd_dist.KVHeadShardedPlan(L, w.table, w.lengths, rank=rank, world=world,
+                                             split_tokens=w.split_tokens)
+            loc = plan.local_layout
+            local = workload.Workload(w.name, loc, w.table, w.lengths, w.split_tokens, dtype=w.dtype,
+                                      std=w.std, seed=w.seed + rank)
+            self.q, self.k, self.v = local.tensors("cuda")
+            self.run = lambda q: plan.run(q, self.k, self.v)
+            self.decode_plan = plan.plan
+            self.bytes_rank = algorithmic_bytes(local)
+            self.sharding = (f"kv_head, strong: rank r owns KV heads [{loc.kv_heads}r, {loc.kv_heads}(r+1)) "
+                             "and their query heads; no collective")
+        else:
+            lt, ll, (lo, hi) = pd_dist.shard_sequence_metadata(w.table, w.lengths, L.page_size, rank, world)
+            ltab, ids = pd_dist.localize_pages(lt, ll, L.page_size)
+            loc = Layout(L.batch, L.query_heads, L.kv_heads, L.head_dim, L.page_size, max(1, len(ids)))
+            local = workload.Workload(w.name, loc, ltab, ll, w.split_tokens, dtype=w.dtype, std=w.std,
+                                      seed=w.seed + rank)
+            plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, split_tokens=w.split_tokens)
+            self.q, self.k, self.v = local.tensors("cuda")
+            self.run = lambda q: plan.run(q, self.k, self.v)
+            self.decode_plan = plan.plan
+            self.bytes_rank = algorithmic_bytes(local)
+            self.extra_kernels = 1                      # the cross-shard merge (NCCL's own kernel not counted)
+            self.nvlink_bytes = plan.nvlink_bytes_per_step
+            self.sharding = (f"sequence, strong: rank r owns logical pages [{lo}, {hi}) of every sequence; "
+                             f"all_gather of {pd_dist.packed_size(loc) * 4} B per rank + max-corrected merge")
+
+    def kernels_per_step(self):
+        return self.decode_plan.kernels_per_run(self.q.dtype) + self.extra_kernels
+
+
+def run_ours(args, rank, local, world):
+    import torch
+
+    job = RankJob(args, rank, world)
+    w = job.workload
+    q, k, v = job.q, job.k, job.v
     kv_bytes = 2 * k.numel() * k.element_size()
     flush = None
     if kv_bytes < 2 * L2_BYTES:
-        flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+        # read-only flush: leaves L2 full of clean lines, so the decode never pays
+        # for write-backs that a zero-fill flush would leave behind
+        flush = torch.ones(2 * L2_BYTES // 2, dtype=torch.float16, device="cuda")
     stream = torch.cuda.current_stream()
 
     def step():
-        return plan.run(q, k, v)
+        return job.run(q)
 
     for _ in range(max(args.warmup, 0)):
         step()
@@ -245,7 +321,7 @@ def run_ours(args, rank, local, world):
         t_start.record(stream)
         for i in range(args.steps):
             if flush is not None:
-                flush.zero_()
+                flush.amax()
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -253,11 +329,11 @@ def run_ours(args, rank, local, world):
         barrier(world)
     launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = t_start.elapsed_time(t_end)
-    if flush is not None:            # flushes sit between steps: count kernel time only
+    if flush is not None:            # flushes sit between steps: count decode time only
         total_ms = sum(launch_ms)
     step_ms = max_over_ranks(total_ms / args.steps, world)
     kernel_ms = statistics.mean(launch_ms)
-    errors = plan.read_errors()
+    errors = job.decode_plan.read_errors()
     if errors:
         raise SystemExit(f"device error word {errors:#x}")
 
@@ -265,11 +341,12 @@ def run_ours(args, rank, local, world):
     e2e = None
     if not args.no_e2e:
         q_host = q.cpu().pin_memory()
-        out_host = torch.empty(plan._out.shape, dtype=torch.float32).pin_memory()
+        out_shape = step().shape
+        out_host = torch.empty(out_shape, dtype=torch.float32).pin_memory()
         q_dev = torch.empty_like(q)
         for _ in range(max(args.warmup, 1)):
             q_dev.copy_(q_host, non_blocking=True)
-            out_host.copy_(plan.run(q_dev, k, v), non_blocking=True)
+            out_host.copy_(job.run(q_dev), non_blocking=True)
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2e_launch = []
@@ -278,10 +355,10 @@ def run_ours(args, rank, local, world):
             if flush is not None:
                 s0 = torch.cuda.Event(enable_timing=True)
                 s1 = torch.cuda.Event(enable_timing=True)
-                flush.zero_()
+                flush.amax()
                 s0.record(stream)
             q_dev.copy_(q_host, non_blocking=True)
-            out_host.copy_(plan.run(q_dev, k, v), non_blocking=True)
+            out_host.copy_(job.run(q_dev), non_blocking=True)
             if flush is not None:
                 s1.record(stream)
                 e2e_launch.append((s0, s1))
@@ -291,18 +368,19 @@ def run_ours(args, rank, local, world):
         if flush is not None:
             e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_launch) / args.steps
         e2e_ms = max_over_ranks(e2e_ms, world)
-        e2e = {"value": world * nbytes / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
+        e2e = {"value": job.bytes_total / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
                "us_per_step": e2e_ms * 1e3,
                "h2d_bytes_per_step": q.numel() * q.element_size(),
                "d2h_bytes_per_step": out_host.numel() * 4,
-               "path": "DecodePlan.run (ctypes -> C ABI pd_decode) with pinned host q/out"}
+               "path": "public API run() (ctypes -> C ABI pd_decode) with pinned host q in, FP32 out back"}
 
     peak, peak_kind = measured_peak()
-    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
-    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+    achieved = job.bytes_rank / (kernel_ms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get(args.workload) if world == 1 else None
+    info = job.decode_plan.native_info(q.dtype)
     line = {
         "metric": METRIC,
-        "value": world * nbytes / (step_ms * 1e-3) / 1e12,
+        "value": job.bytes_total / (step_ms * 1e-3) / 1e12,
         "unit": "TB/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -310,32 +388,32 @@ def run_ours(args, rank, local, world):
         "ms_per_step": step_ms,
         "us_per_step": step_ms * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if (world == 1 or args.scaling == "weak") else "strong",
         "vs_baseline": None,
         "dtype": "f16" if w.dtype == "float16" else "f32",
         "data": "synthetic: seeded N(0,1) tensors, BASELINE config generators (no dataset exists)",
         "config": {"workload": w.name, "batch": w.layout.batch, "query_heads": w.layout.query_heads,
                    "kv_heads": w.layout.kv_heads, "head_dim": w.layout.head_dim,
                    "page_size": w.layout.page_size, "split_tokens": w.split_tokens,
-                   "bytes_per_step_per_gpu": nbytes,
-                   "sharding": ("none" if world == 1 else
-                                f"kv_head, weak: rank r owns KV heads [8r, 8r+8) of a {8 * world}-KV-head "
-                                "model, same sequences on every rank, no collective"),
-                   "l2": ("inputs larger than L2" if flush is None else "L2 flushed between steps"),
-                   "persistent_ctas": plan.num_ctas,
-                   "kv_heads_per_tile": int(plan.native_info(q.dtype).heads_per_tile)},
+                   "bytes_per_step_total": job.bytes_total, "bytes_per_step_rank": job.bytes_rank,
+                   "sharding": job.sharding,
+                   "l2": ("inputs larger than L2" if flush is None else "L2 flushed (read-only) between steps"),
+                   "persistent_ctas": int(info.num_ctas),
+                   "kv_heads_per_tile": int(info.heads_per_tile)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "kernel": "paged_decode_kernel",
+                     "traffic": traffic, "kernel": "paged_decode_kernel (+ merge_partials_kernel)",
                      "kernel_us": kernel_ms * 1e3,
-                     "algorithmic_bytes_per_launch": nbytes},
-        "gpu_launches": args.steps * plan.kernels_per_run(q.dtype),
+                     "algorithmic_bytes_per_launch": job.bytes_rank},
+        "gpu_launches": args.steps * job.kernels_per_step(),
         "clocks": clocks.summary(),
     }
+    if hasattr(job, "nvlink_bytes"):
+        line["nvlink_bytes_per_step_per_gpu"] = job.nvlink_bytes
     if e2e:
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(w, q, k, v, nbytes, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(w, q, k, v, job.bytes_total, args.cpu_seconds)
     return line
 
 

@@ -138,12 +138,18 @@ pd_status pd_decode_with_stats(pd_plan *plan, const void *q, const void *k, cons
                                pd_dtype dtype, float *out, float *stats, void *stream);
 
 /* Max-corrected merge of per-shard results (the merge algebra of
- * oracle.py:88-96 applied across shards): shard_out [shards, rows, head_dim]
- * and shard_stats [shards, rows, 2] as written by pd_decode_with_stats,
+ * oracle.py:88-96 applied across shards), as written by pd_decode_with_stats.
+ * Shard s's normalised outputs (rows x head_dim floats) start at
+ * shard_out + s * shard_stride and its (m, l) pairs (rows x 2 floats) at
+ * shard_stats + s * shard_stride; shard_stride counts floats.  For one packed
+ * buffer per shard ([rows * head_dim outputs][rows * 2 stats], the layout the
+ * sequence-sharded all-gather produces) pass shard_stats = shard_out +
+ * rows * head_dim and shard_stride = rows * (head_dim + 2).  Writes
  * out [rows, head_dim].  Device pointers on the current device.
  */
 pd_status pd_merge_shards(const float *shard_out, const float *shard_stats, int32_t shards,
-                          int64_t rows, int32_t head_dim, float *out, void *stream);
+                          int64_t shard_stride, int64_t rows, int32_t head_dim, float *out,
+                          void *stream);
 
 /* Debug gather through the decode kernel's own TMA page path: writes the
  * live K and V rows of every (sequence, KV head) as dense

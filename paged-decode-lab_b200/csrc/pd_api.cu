@@ -282,14 +282,20 @@ PD_API pd_status pd_decode_with_stats(pd_plan *p, const void *q, const void *k, 
 }
 
 PD_API pd_status pd_merge_shards(const float *shard_out, const float *shard_stats, int32_t shards,
-                                 int64_t rows, int32_t head_dim, float *out, void *stream) {
+                                 int64_t shard_stride, int64_t rows, int32_t head_dim, float *out,
+                                 void *stream) {
     if (!shard_out || !shard_stats || !out) return fail(PD_ERR_VALUE, "pointers must not be NULL");
-    if (shards < 1 || rows < 0 || head_dim <= 0)
-        return fail(PD_ERR_VALUE, "shards >= 1, rows >= 0 and head_dim > 0 required");
+    if (shards < 1 || rows < 0 || head_dim <= 0 || (head_dim & 31))
+        return fail(PD_ERR_VALUE, "shards >= 1, rows >= 0 and head_dim a positive multiple of 32 required");
+    if (shards > 1 && shard_stride < rows * head_dim)
+        return fail(PD_ERR_VALUE, "shard_stride must cover a shard's rows * head_dim outputs");
+    if (reinterpret_cast<uintptr_t>(shard_stats) & 7)
+        return fail(PD_ERR_VALUE, "shard_stats must be 8-byte aligned");
     if (rows == 0) return PD_OK;
     if ((rows + 7) / 8 > INT32_MAX) return fail(PD_ERR_VALUE, "too many rows");
     const cudaError_t err =
-        launch_merge_shards(shard_out, shard_stats, shards, rows, head_dim, out, static_cast<cudaStream_t>(stream));
+        launch_merge_shards(shard_out, shard_stats, shards, shard_stride, rows, head_dim, out,
+                            static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
     return PD_OK;

@@ -101,8 +101,8 @@ cudaError_t launch_merge_partials(const DecodeArgs &args, int hg, int gt, int ns
                                   cudaStream_t stream);
 
 // Max-corrected merge of [shards, rows, D] shard outputs (pd_merge.cu).
-cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t rows,
-                                int D, float *out, cudaStream_t stream);
+cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t stride,
+                                int64_t rows, int D, float *out, cudaStream_t stream);
 
 // Defined in the per-shape translation units.
 KernelEntry kernel_entry_f16_d64_t16(int gt, int hg, int mode);

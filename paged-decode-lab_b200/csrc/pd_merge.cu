@@ -6,28 +6,29 @@ namespace pd {
 // ------------------------------------------------------------------ cross-shard merge
 // out[row] = sum_s exp2(m_s - M) * l_s * o_s / sum_s exp2(m_s - M) * l_s over shards
 // with l_s > 0 (o_s is each shard's normalised output); zero when all are empty.
+// Shard s's rows start at shard_out + s * stride and shard_stats + s * stride.
 static __global__ void merge_shards_kernel(const float *__restrict__ shard_out,
-                                    const float2 *__restrict__ shard_stats, int shards, int64_t rows,
-                                    int D, float *__restrict__ out) {
+                                    const float *__restrict__ shard_stats, int shards, int64_t stride,
+                                    int64_t rows, int D, float *__restrict__ out) {
     const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     float top = -INFINITY;
     for (int s = 0; s < shards; ++s) {
-        const float2 ml = shard_stats[int64_t(s) * rows + row];
+        const float2 ml = *reinterpret_cast<const float2 *>(shard_stats + int64_t(s) * stride + 2 * row);
         if (ml.y > 0.f) top = fmaxf(top, ml.x);
     }
     float den = 0.f;
     for (int s = 0; s < shards; ++s) {
-        const float2 ml = shard_stats[int64_t(s) * rows + row];
+        const float2 ml = *reinterpret_cast<const float2 *>(shard_stats + int64_t(s) * stride + 2 * row);
         if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
     }
     for (int d = lane; d < D; d += 32) {
         float num = 0.f;
         for (int s = 0; s < shards; ++s) {
-            const float2 ml = shard_stats[int64_t(s) * rows + row];
+            const float2 ml = *reinterpret_cast<const float2 *>(shard_stats + int64_t(s) * stride + 2 * row);
             if (ml.y > 0.f)
-                num = fmaf(exp2f(ml.x - top) * ml.y, shard_out[(int64_t(s) * rows + row) * D + d], num);
+                num = fmaf(exp2f(ml.x - top) * ml.y, shard_out[int64_t(s) * stride + row * D + d], num);
         }
         out[row * D + d] = den > 0.f ? num / den : 0.f;
     }
@@ -69,12 +70,12 @@ cudaError_t launch_merge_partials(const DecodeArgs &args, int hg, int gt, int ns
     }
 }
 
-cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t rows,
-                                int D, float *out, cudaStream_t stream) {
+cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats, int shards, int64_t stride,
+                                int64_t rows, int D, float *out, cudaStream_t stream) {
     constexpr int kRowsPerBlock = 8;
     const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-    merge_shards_kernel<<<unsigned(blocks), kRowsPerBlock * 32, 0, stream>>>(
-        shard_out, reinterpret_cast<const float2 *>(shard_stats), shards, rows, D, out);
+    merge_shards_kernel<<<unsigned(blocks), kRowsPerBlock * 32, 0, stream>>>(shard_out, shard_stats, shards,
+                                                                             stride, rows, D, out);
     return cudaGetLastError();
 }
 

@@ -45,7 +45,7 @@ SIGNATURES = {
     "pd_plan_bind": (_c_int32, [_vp, _vp, _c_size, _vp]),
     "pd_decode": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
     "pd_decode_with_stats": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
-    "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int32, _vp, _vp]),
+    "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_plan_read_errors": (_c_int32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "pd_decode_static": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),

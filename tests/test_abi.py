@@ -92,7 +92,7 @@ def test_null_arguments_are_errors_not_crashes():
     assert lib.pd_plan_create(None, None, 0, None, 256, 0, 0, -1, 1, None) == _native.PD_ERR_VALUE
     assert lib.pd_plan_get_info(None, None) == _native.PD_ERR_VALUE
     assert lib.pd_decode(None, None, None, None, 0, None, None) == _native.PD_ERR_VALUE
-    assert lib.pd_merge_shards(None, None, 1, 1, 128, None, None) == _native.PD_ERR_VALUE
+    assert lib.pd_merge_shards(None, None, 1, 0, 1, 128, None, None) == _native.PD_ERR_VALUE
     assert lib.pd_plan_device_bytes(None) == 0
     lib.pd_plan_destroy(None)
 

@@ -81,68 +81,83 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    t = time.time()
+    print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+          pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    time.sleep(0.0005)
+"""
+
+
 class ClockSampler:
     """SM clock and throttle reasons sampled while the timed region runs.
 
-    NVML (the library nvidia-smi reads) is polled every millisecond from a
-    background thread, so even a few-millisecond timed region gets samples;
-    falls back to `nvidia-smi -lms 200` when NVML is unavailable.
+    A child process polls NVML (the library nvidia-smi reads) every half
+    millisecond, free of this process's GIL; `mark_start`/`mark_end` bracket
+    the timed region in wall-clock time and only samples inside it count.
     """
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
 
-    def __init__(self, device_index, period_s=0.001):
+    def __init__(self, device_index):
         self.device_index = device_index
-        self.period_s = period_s
-        self.samples = []
-        self.max_mhz = None
-        self._stop = None
-
-    def __enter__(self):
-        import threading
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            handle = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index())
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
-        except Exception:  # noqa: BLE001 - NVML missing: no samples, reported as such
-            return self
-        self._stop = threading.Event()
-
-        def poll():
-            while not self._stop.is_set():
-                try:
-                    mhz = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
-                    reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                    self.samples.append((mhz, reasons))
-                except Exception:  # noqa: BLE001
-                    pass
-                self._stop.wait(self.period_s)
-        self._thread = threading.Thread(target=poll, daemon=True)
-        self._thread.start()
-        return self
+        self.proc = None
+        self.t0 = self.t1 = None
+        self.rows, self.max_mhz = [], None
 
     def _physical_index(self):
         visible = os.environ.get("CUDA_VISIBLE_DEVICES")
         if visible:
-            ids = [x for x in visible.split(",") if x.strip()]
-            if self.device_index < len(ids) and ids[self.device_index].strip().isdigit():
+            ids = [x.strip() for x in visible.split(",") if x.strip()]
+            if self.device_index < len(ids) and ids[self.device_index].isdigit():
                 return int(ids[self.device_index])
         return self.device_index
 
-    def __exit__(self, *exc):
-        if self._stop is not None:
-            self._stop.set()
-            self._thread.join(timeout=2)
-        return False
+    def start(self):
+        try:
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self._physical_index())],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline().split()   # "max <mhz>" once NVML is up
+            self.max_mhz = int(first[1]) if len(first) == 2 else None
+        except Exception:  # noqa: BLE001 - no NVML: reported as unsampled
+            self.proc = None
+        return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
+        if not self.proc:
+            return
+        time.sleep(0.002)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.splitlines():
+            parts = line.split()
+            if len(parts) == 3:
+                t, mhz, reasons = float(parts[0]), int(parts[1]), int(parts[2])
+                if self.t0 is not None and self.t0 <= t <= (self.t1 or t):
+                    self.rows.append((mhz, reasons))
 
     def summary(self):
-        if not self.samples:
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
-        reasons = sorted(name for name, bit in self.REASONS.items()
-                         if any(r & bit for _, r in self.samples))
-        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.rows))
+        return {"sm_mhz": statistics.median(m for m, _ in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 0.5 ms"}
 
 
 def algorithmic_bytes(w):
@@ -308,6 +323,7 @@ def run_ours(args, rank, local, world):
     def step():
         return job.run(q)
 
+    clocks = ClockSampler(local).start()
     for _ in range(max(args.warmup, 0)):
         step()
     barrier(world)
@@ -316,17 +332,19 @@ def run_ours(args, rank, local, world):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        barrier(world)
-        t_start.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.amax()
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        t_end.record(stream)
-        barrier(world)
+    barrier(world)
+    clocks.mark_start()
+    t_start.record(stream)
+    for i in range(args.steps):
+        if flush is not None:
+            flush.amax()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    t_end.record(stream)
+    barrier(world)
+    clocks.mark_end()
+    clocks.stop()
     launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = t_start.elapsed_time(t_end)
     if flush is not None:            # flushes sit between steps: count decode time only
@@ -337,42 +355,68 @@ def run_ours(args, rank, local, world):
     if errors:
         raise SystemExit(f"device error word {errors:#x}")
 
-    # (2) e2e through the public API with host buffers
+    # (2) e2e through the public API with host buffers.  Every step copies its q
+    # from pinned host memory and its FP32 output back; copies run on a side
+    # stream, double-buffered, so step i's copies overlap steps i-1 / i+1.
     e2e = None
     if not args.no_e2e:
-        q_host = q.cpu().pin_memory()
+        copy = torch.cuda.Stream()
+        q_host = [q.cpu().pin_memory() for _ in range(2)]
         out_shape = step().shape
-        out_host = torch.empty(out_shape, dtype=torch.float32).pin_memory()
-        q_dev = torch.empty_like(q)
-        for _ in range(max(args.warmup, 1)):
-            q_dev.copy_(q_host, non_blocking=True)
-            out_host.copy_(job.run(q_dev), non_blocking=True)
+        out_host = [torch.empty(out_shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+        q_dev = [torch.empty_like(q) for _ in range(2)]
+        stage = [torch.empty(out_shape, dtype=torch.float32, device=q.device) for _ in range(2)]
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
+        computed = [torch.cuda.Event() for _ in range(2)]
+        d2h_done = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_step(i):
+            b = i % 2
+            with torch.cuda.stream(copy):
+                copy.wait_event(computed[b])          # q_dev[b] no longer read by step i-2
+                q_dev[b].copy_(q_host[b], non_blocking=True)
+                h2d_done[b].record(copy)
+            stream.wait_event(h2d_done[b])
+            stream.wait_event(d2h_done[b])            # stage[b] drained by step i-2's copy
+            stage[b].copy_(job.run(q_dev[b]))
+            computed[b].record(stream)
+            with torch.cuda.stream(copy):
+                copy.wait_event(computed[b])
+                out_host[b].copy_(stage[b], non_blocking=True)
+                d2h_done[b].record(copy)
+
+        for i in range(max(args.warmup, 2)):
+            e2e_step(i)
+        torch.cuda.synchronize()
         barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2e_launch = []
+        t0 = time.perf_counter()
+        e0 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
             if flush is not None:
-                s0 = torch.cuda.Event(enable_timing=True)
-                s1 = torch.cuda.Event(enable_timing=True)
                 flush.amax()
-                s0.record(stream)
-            q_dev.copy_(q_host, non_blocking=True)
-            out_host.copy_(job.run(q_dev), non_blocking=True)
-            if flush is not None:
-                s1.record(stream)
-                e2e_launch.append((s0, s1))
+            e2e_step(i)
+        stream.wait_stream(copy)
+        e1 = torch.cuda.Event(enable_timing=True)
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / args.steps
-        if flush is not None:
-            e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_launch) / args.steps
+        if flush is not None:                     # take out the flushes' own time
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(args.steps):
+                flush.amax()
+            f1.record(stream)
+            torch.cuda.synchronize()
+            e2e_ms -= f0.elapsed_time(f1) / args.steps
         e2e_ms = max_over_ranks(e2e_ms, world)
         e2e = {"value": job.bytes_total / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
                "us_per_step": e2e_ms * 1e3,
                "h2d_bytes_per_step": q.numel() * q.element_size(),
-               "d2h_bytes_per_step": out_host.numel() * 4,
-               "path": "public API run() (ctypes -> C ABI pd_decode) with pinned host q in, FP32 out back"}
+               "d2h_bytes_per_step": out_host[0].numel() * 4,
+               "wall_s": time.perf_counter() - t0,
+               "path": "public API run() (ctypes -> C ABI pd_decode); pinned host q in and FP32 out back "
+                       "every step on a side stream, double-buffered"}
 
     peak, peak_kind = measured_peak()
     achieved = job.bytes_rank / (kernel_ms * 1e-3) / 1e9

@@ -50,9 +50,10 @@ METRIC = "decode-attn µs/step + achieved HBM TB/s vs ~8 TB/s peak at 1/2/4/8 B2
 L2_BYTES = 126 * 2**20
 DEFAULT_STEPS, DEFAULT_WARMUP = 50, 5
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the decode kernel,
-# from the ncu captures summarised in profiles/ (None until captured).
-NCU_TRAFFIC_BYTES = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch, from
+# the ncu captures summarised in profiles/paged_decode_kernel_config2.md
+# (launch 0 of each capture; None for workloads not captured).
+NCU_TRAFFIC_BYTES = {"c2": 468_802_560 + 4_160_512, "c5": 1_073_926_912 + 5_157_376}
 
 
 def parse_args():

@@ -48,7 +48,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode-attn µs/step + achieved HBM TB/s vs ~8 TB/s peak at 1/2/4/8 B200"
 L2_BYTES = 126 * 2**20
-DEFAULT_STEPS, DEFAULT_WARMUP = 50, 5
+DEFAULT_STEPS, DEFAULT_WARMUP = 200, 5
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch, from
 # the ncu captures summarised in profiles/paged_decode_kernel_config2.md
@@ -110,7 +110,7 @@ class ClockSampler:
         self.device_index = device_index
         self.proc = None
         self.t0 = self.t1 = None
-        self.rows, self.max_mhz = [], None
+        self.rows, self.max_mhz, self.window = [], None, None
 
     def _physical_index(self):
         visible = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -146,19 +146,27 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        samples = []
         for line in out.splitlines():
             parts = line.split()
             if len(parts) == 3:
-                t, mhz, reasons = float(parts[0]), int(parts[1]), int(parts[2])
-                if self.t0 is not None and self.t0 <= t <= (self.t1 or t):
-                    self.rows.append((mhz, reasons))
+                samples.append((float(parts[0]), int(parts[1]), int(parts[2])))
+        t0, t1 = self.t0 or 0.0, self.t1 or float("inf")
+        self.rows = [(m, r) for t, m, r in samples if t0 <= t <= t1]
+        self.window = "timed region"
+        if not self.rows:
+            # a very short timed region can fall between two polls: use the polls
+            # just around it (the GPU runs the same steps back to back there too)
+            self.rows = [(m, r) for t, m, r in samples if t0 - 0.05 <= t <= t1 + 0.05]
+            self.window = "timed region +- 50 ms"
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
         reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.rows))
         return {"sm_mhz": statistics.median(m for m, _ in self.rows), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 0.5 ms"}
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 0.5 ms",
+                "window": self.window}
 
 
 def algorithmic_bytes(w):

@@ -22,11 +22,9 @@ struct KernelEntry {
 };
 
 // Shape of one kernel: HG KV heads per page tile and NSUB sub-pipelines of
-// HG consumer warps each.  NSUB starts at NC0 / HG (NC0 = 8 consumer warps,
-// 4 when 32 query heads share a KV head: their accumulators take 128
-// registers per thread) and halves until at least NSUB page tiles fit in
-// shared memory next to the merge buffers; the ring then takes as many slots
-// as fit, rounded down to a multiple of NSUB.
+// HG consumer warps each.  NSUB starts at max_sub_pipelines() and halves
+// until at least NSUB page tiles fit in shared memory; the ring then takes as
+// many slots as fit, rounded down to a multiple of NSUB.
 template <typename Elt, int D, int T, int GT, int HG, int NSUB>
 struct RingFit {
     using Probe = KernelShape<Elt, D, T, GT, HG, NSUB, NSUB>;
@@ -51,8 +49,7 @@ struct PickSub<Elt, D, T, GT, HG, 1> {
 
 template <typename Elt, int D, int T, int GT, int HG>
 struct LaunchShape {
-    static constexpr int NC0 = GT == 32 ? 4 : 8;
-    static constexpr int NSUB = PickSub<Elt, D, T, GT, HG, (NC0 / HG > 0 ? NC0 / HG : 1)>::value;
+    static constexpr int NSUB = PickSub<Elt, D, T, GT, HG, max_sub_pipelines(sizeof(Elt), HG, GT)>::value;
     static constexpr int SLOTS = RingFit<Elt, D, T, GT, HG, NSUB>::SLOTS;
     static_assert(SLOTS >= NSUB && SLOTS >= 1, "a page tile does not fit in shared memory");
 };

@@ -17,4 +17,14 @@ inline int choose_heads_per_tile(int elt, int D, int T, int GT, int kv_heads, in
     return best;
 }
 
+// Sub-pipelines a kernel shape starts from (it may use fewer when its page
+// tiles leave room for fewer ring slots): consumer warps are HG * NSUB.  FP16
+// tiles with at least 4 KV heads keep 4-8 warps busy with NSUB = 1 (one warp
+// per head sees the whole group, so unsplit groups need no merge); otherwise
+// NC0 / HG sub-pipelines fill NC0 warps (8, or 4 when 32 query heads share a
+// KV head).
+inline constexpr int max_sub_pipelines(int elt, int hg, int gt) {
+    return (elt == 2 && hg >= 4) ? 1 : ((gt == 32 ? 4 : 8) / hg > 0 ? (gt == 32 ? 4 : 8) / hg : 1);
+}
+
 }  // namespace pd

@@ -175,12 +175,11 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         cursor = end;
     }
     // Partial slots.  A segment's consumer warps run as NSUB sub-pipelines
-    // (NSUB <= NC0 / HG, fewer when a kernel's tiles leave room for fewer
-    // slots), each writing its own partial; slot_stride = NC0 / HG slots are
-    // reserved per segment.  A group with one segment and slot_stride == 1 is
+    // (NSUB <= max_sub_pipelines(), fewer when a kernel's tiles leave room for
+    // fewer slots), each writing its own partial; slot_stride =
+    // max_sub_pipelines() slots are reserved per segment.  A group with one segment and slot_stride == 1 is
     // seen whole by one warp per head, which writes the final output itself.
-    const int nc0 = p.group_tile == 32 ? 4 : 8;
-    p.slot_stride = std::max(1, nc0 / hg);
+    p.slot_stride = max_sub_pipelines(dtype == PD_FLOAT16 ? 2 : 4, hg, p.group_tile);
     std::vector<int32_t> next_slot(ngroups, -1);
     int64_t slots = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) {

@@ -46,7 +46,8 @@ def check_worklist(layout, table, lengths, plan):
     if total:
         assert min(per_cta) >= total // C and max(per_cta) <= -(-total // C)
     stride = info["slot_stride"]
-    assert stride == max(1, (4 if gt == 32 else 8) // hg)
+    # FP16 plans: one sub-pipeline once 4+ heads share a tile, else 8 (4 for GT 32) warps' worth
+    assert stride == (1 if hg >= 4 else max(1, (4 if gt == 32 else 8) // hg))
     covered = {gi: [] for gi in range(len(groups))}
     for c in range(C):
         for s in segs[offs[c]:offs[c + 1]]:

@@ -14,12 +14,13 @@
 //     HG heads at once because a TMA instruction costs the same ~75 issue
 //     cycles whatever its size; many bytes per instruction keep one thread
 //     ahead of HBM;
-//   * consumer warp w owns KV head w % HG of the group and takes every
-//     NSUB-th tile (NSUB = NC / HG); it folds its tiles into an online
-//     softmax (running max m, denominator l, unnormalised output o) for all
-//     query heads of that KV head at once: FP16 inputs use m16n8k16
-//     tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T, FP32 accumulators), FP32
-//     inputs use FP32 FMAs;
+//   * a consumer warp owns one KV head of the group and a slice of 8 of its
+//     query heads (QT = GT / 8 slices; wide groups such as MQA split their
+//     query heads over warps that read the same tile) and takes every NSUB-th
+//     tile; it folds its tiles into an online softmax (running max m,
+//     denominator l, unnormalised output o) for its 8 query heads: FP16
+//     inputs use m16n8k16 tensor-core MMAs (S^T = K Q^T, O^T += V^T P^T, FP32
+//     accumulators), FP32 inputs use FP32 FMAs;
 //   * consumer warps never wait for each other: at the end of its share of
 //     a segment a warp writes its heads' normalised output directly when it
 //     alone saw the whole group (one segment, NSUB == 1), else an (m, l, o)
@@ -62,7 +63,9 @@ constexpr uint32_t kErrBadPage = 2u;
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS>
 struct KernelShape {
     static constexpr int ELT = sizeof(Elt);
-    static constexpr int NC = HG * NSUB;               // consumer warps
+    static constexpr int QT = GT / 8;                  // 8-query-head slices per KV head
+    static constexpr int CPT = HG * QT;                // consumer warps reading each tile
+    static constexpr int NC = CPT * NSUB;              // consumer warps
     static constexpr int ROW_BYTES = D * ELT;
     static constexpr int NBOX = ROW_BYTES / 128;       // 128-byte TMA boxes per token row
     static constexpr int BOX_ELEMS = 128 / ELT;
@@ -71,10 +74,10 @@ struct KernelShape {
     static constexpr int TILE_BYTES = 2 * HALF_BYTES;
     static constexpr int THREADS = (NC + 1) * 32;
     static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
-    // FP16 with up to 16 query heads per KV head keeps Q in registers;
-    // otherwise every consumer warp stages its heads' Q in its own slice.
-    static constexpr bool Q_SMEM = !(ELT == 2 && GT <= 16);
-    static constexpr size_t QS = Q_SMEM ? size_t(NC) * GT * D * ELT : 0;
+    // FP16 keeps each warp's 8 query heads in registers; FP32 stages them in
+    // the warp's own shared-memory slice.
+    static constexpr bool Q_SMEM = ELT != 2;
+    static constexpr size_t QS = Q_SMEM ? size_t(NC) * 8 * D * ELT : 0;
     static constexpr size_t BARS = size_t(SLOTS) * 16;
     static constexpr size_t FLAGS = size_t(SLOTS) * 4 + 16;
     static constexpr size_t SMEM = 1024 + RING + QS + BARS + FLAGS;
@@ -423,7 +426,7 @@ struct EngineFor<float, D, T, GT, ROWS> {
 enum : int { kModeDecode = 0, kModeGather = 1 };
 
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS, int MODE>
-__global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
+__global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
     using S = KernelShape<Elt, D, T, GT, HG, NSUB, SLOTS>;
@@ -454,7 +457,7 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < SLOTS; ++s) {
             mbar_init(smem_u32(full_bar + s), 1);
-            mbar_init(smem_u32(empty_bar + s), HG);   // released by the HG warps that read it
+            mbar_init(smem_u32(empty_bar + s), S::CPT);   // released by the warps that read it
         }
         flags->abort = 0;
         mbar_init_fence();
@@ -514,8 +517,9 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
     }
 
     // ---------------------------------------------------------------- consumers
-    const int hh = warp % HG;       // KV head of the group this warp owns
-    const int sub = warp / HG;      // this warp takes tiles j with j % NSUB == sub
+    const int hh = warp % S::CPT / S::QT;   // KV head of the group this warp owns
+    const int qt = warp % S::QT;            // its 8-query-head slice of that head
+    const int sub = warp / S::CPT;          // it takes tiles j with j % NSUB == sub
     const int r0 = hh * T;          // its rows in a [head][token] tile
     bool stop = false;
     int j = 0;
@@ -559,23 +563,23 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
             }
             j += npg;
         } else {
-            using Engine = typename EngineFor<Elt, D, T, GT, S::ROWS>::type;
+            using Engine = typename EngineFor<Elt, D, T, 8, S::ROWS>::type;
             Engine eng;
-            // query heads of this warp's KV head: (kv0 + hh) * G + qoff + g, g < nh
-            const int64_t qhead0 = int64_t(b) * a.Hq + int64_t(kv0 + hh) * a.group + qoff;
+            // this warp's query heads: (kv0 + hh) * G + qoff + qt * 8 + g, g < nw
+            const int nw = min(8, nh - qt * 8);     // may be <= 0: the warp then idles on its tiles
+            const int64_t qhead0 = int64_t(b) * a.Hq + int64_t(kv0 + hh) * a.group + qoff + qt * 8;
             const Elt *qrow = static_cast<const Elt *>(a.q) + qhead0 * D;
-            uint8_t *qmine = qsm + size_t(warp) * GT * D * sizeof(Elt);
+            uint8_t *qmine = qsm + size_t(warp) * 8 * D * sizeof(Elt);
             const uint32_t qs = smem_u32(qmine);
-            static_assert(!std::is_same<Elt, __half>::value ||
-                              S::Q_SMEM == !HalfEngine<D, T, GT, S::ROWS>::Q_REGS,
-                          "Q staging must match the FP16 engine");
+            static_assert(!std::is_same<Elt, __half>::value || HalfEngine<D, T, 8, S::ROWS>::Q_REGS,
+                          "FP16 warps keep their 8 query heads in registers");
             if constexpr (S::Q_SMEM) {
                 // this warp's Q rows (zero rows for heads past nh) into its own slice
                 constexpr int CPR = D * int(sizeof(Elt)) / 16;
-                for (int e = lane; e < GT * CPR; e += 32) {
+                for (int e = lane; e < 8 * CPR; e += 32) {
                     const int g = e / CPR, c = e % CPR;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (g < nh) v = __ldg(reinterpret_cast<const float4 *>(qrow + int64_t(g) * D) + c);
+                    if (g < nw) v = __ldg(reinterpret_cast<const float4 *>(qrow + int64_t(g) * D) + c);
                     // FP16 rows are read by ldmatrix: swizzle 16-byte chunks by row
                     const int sc = std::is_same<Elt, __half>::value ? ((c & 8) | ((c & 7) ^ (g & 7))) : c;
                     reinterpret_cast<float4 *>(qmine + size_t(g) * D * sizeof(Elt))[sc] = v;
@@ -583,9 +587,9 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
                 __syncwarp();
             }
             if constexpr (std::is_same<Elt, __half>::value)
-                eng.begin(reinterpret_cast<const __half *>(qrow), nh, lane, qs);
+                eng.begin(reinterpret_cast<const __half *>(qrow), nw, lane, qs);
             else
-                eng.begin(nh, lane, qs);
+                eng.begin(nw, lane, qs);
 
             for (int t = first; t < npg; t += NSUB) {
                 const int jj = j + t;
@@ -612,19 +616,19 @@ __global__ void __launch_bounds__((HG * NSUB + 1) * 32, 1)
             if (sg.w < 0) {
                 // the group's only segment and the only warp of this head: final output
                 eng.for_each_o([&](int g, int d, float o, float, float l) {
-                    if (g < nh) a.out[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
+                    if (g < nw) a.out[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
                 });
                 if (a.stats)
                     eng.for_each_ml([&](int g, float m, float l) {
-                        if (g < nh) reinterpret_cast<float2 *>(a.stats)[qhead0 + g] = make_float2(m, l);
+                        if (g < nw) reinterpret_cast<float2 *>(a.stats)[qhead0 + g] = make_float2(m, l);
                     });
             } else {
                 const int64_t ps = (int64_t(sg.w) + sub) * HG + hh;   // [slot][head] partial row
                 eng.for_each_o([&](int g, int d, float o, float, float) {
-                    if (g < nh) a.part_o[(ps * GT + g) * D + d] = o;
+                    if (g < nw) a.part_o[(ps * GT + qt * 8 + g) * D + d] = o;
                 });
                 eng.for_each_ml([&](int g, float m, float l) {
-                    if (g < nh) a.part_ml[ps * GT + g] = make_float2(m, l);
+                    if (g < nw) a.part_ml[ps * GT + qt * 8 + g] = make_float2(m, l);
                 });
             }
         }

@@ -49,7 +49,7 @@ struct PickSub<Elt, D, T, GT, HG, 1> {
 
 template <typename Elt, int D, int T, int GT, int HG>
 struct LaunchShape {
-    static constexpr int NSUB = PickSub<Elt, D, T, GT, HG, max_sub_pipelines(sizeof(Elt), HG, GT)>::value;
+    static constexpr int NSUB = PickSub<Elt, D, T, GT, HG, max_sub_pipelines(sizeof(Elt), HG, GT, D, T)>::value;
     static constexpr int SLOTS = RingFit<Elt, D, T, GT, HG, NSUB>::SLOTS;
     static_assert(SLOTS >= NSUB && SLOTS >= 1, "a page tile does not fit in shared memory");
 };
@@ -64,12 +64,15 @@ KernelEntry make_entry() {
 
 // KV heads per tile are instantiated while an FP16 page tile (K + V of HG
 // heads) stays within 64 KiB, so the FP32 tile (twice as large) still fits
-// in shared memory; the planner never asks for more (choose_heads_per_tile).
-constexpr bool heads_per_tile_allowed(int D, int T, int hg) { return 4 * D * T * hg <= 65536; }
+// in shared memory, and while a tile has at most 8 consumer warps; the
+// planner never asks for more (choose_heads_per_tile).
+constexpr bool heads_per_tile_allowed(int D, int T, int GT, int hg) {
+    return 4 * D * T * hg <= 65536 && tile_consumers(hg, GT) <= 8;
+}
 
 template <typename Elt, int D, int T, int GT, int HG, int MODE>
 KernelEntry entry_clamped() {
-    if constexpr (HG > 1 && !heads_per_tile_allowed(D, T, HG))
+    if constexpr (HG > 1 && !heads_per_tile_allowed(D, T, GT, HG))
         return entry_clamped<Elt, D, T, GT, HG / 2, MODE>();
     else
         return make_entry<Elt, D, T, GT, HG, MODE>();
@@ -78,7 +81,7 @@ KernelEntry entry_clamped() {
 template <typename Elt, int D, int T, int GT, int MODE>
 KernelEntry entry_for_hg(int hg) {
     switch (hg) {
-        case 8: return entry_clamped<Elt, D, T, GT, (GT == 32 ? 4 : 8), MODE>();
+        case 8: return entry_clamped<Elt, D, T, GT, 8, MODE>();
         case 4: return entry_clamped<Elt, D, T, GT, 4, MODE>();
         case 2: return entry_clamped<Elt, D, T, GT, 2, MODE>();
         default: return entry_clamped<Elt, D, T, GT, 1, MODE>();

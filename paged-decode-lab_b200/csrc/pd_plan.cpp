@@ -179,7 +179,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // fewer slots), each writing its own partial; slot_stride =
     // max_sub_pipelines() slots are reserved per segment.  A group with one segment and slot_stride == 1 is
     // seen whole by one warp per head, which writes the final output itself.
-    p.slot_stride = max_sub_pipelines(dtype == PD_FLOAT16 ? 2 : 4, hg, p.group_tile);
+    p.slot_stride = max_sub_pipelines(dtype == PD_FLOAT16 ? 2 : 4, hg, p.group_tile, L.head_dim, T);
     std::vector<int32_t> next_slot(ngroups, -1);
     int64_t slots = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) {

@@ -27,7 +27,7 @@ def check_worklist(layout, table, lengths, plan):
     gt = info["group_tile"]
     assert gt == (8 if G <= 8 else 16 if G <= 16 else 32)
     hg = info["heads_per_tile"]
-    assert hg in (1, 2, 4, 8) and layout.kv_heads % hg == 0 and hg <= (4 if gt == 32 else 8)
+    assert hg in (1, 2, 4, 8) and layout.kv_heads % hg == 0 and hg * gt // 8 <= 8
     # FP16 page tile (K + V of hg heads) within the 64 KiB target unless hg == 1
     assert hg == 1 or hg * 2 * layout.head_dim * 2 * T <= 64 * 1024
     splits = math.ceil(G / gt)
@@ -46,8 +46,12 @@ def check_worklist(layout, table, lengths, plan):
     if total:
         assert min(per_cta) >= total // C and max(per_cta) <= -(-total // C)
     stride = info["slot_stride"]
-    # FP16 plans: one sub-pipeline once 4+ heads share a tile, else 8 (4 for GT 32) warps' worth
-    assert stride == (1 if hg >= 4 else max(1, (4 if gt == 32 else 8) // hg))
+    # FP16 plans: consumer warps per tile = hg * gt/8 <= 8; sub-pipelines by tile size
+    cpt = hg * gt // 8
+    assert cpt <= 8
+    tile = 2 * layout.head_dim * 2 * T * hg
+    want = 1 if tile >= 32768 else min(2 if tile >= 16384 else 4, 8 // cpt)
+    assert stride == max(1, want)
     covered = {gi: [] for gi in range(len(groups))}
     for c in range(C):
         for s in segs[offs[c]:offs[c + 1]]:

@@ -319,49 +319,61 @@ struct FloatEngine {
         }
     }
 
+    // The head count is dispatched to a compile-time bound so that an MHA
+    // warp (one query head) runs no code for the seven unused head slots.
     __device__ __forceinline__ void tile(uint32_t kbase, int r0, int valid, float scale_log2) {
+        switch (nh) {
+            case 1: tile_n<1>(kbase, r0, valid, scale_log2); break;
+            case 2: tile_n<2>(kbase, r0, valid, scale_log2); break;
+            case 3: tile_n<3>(kbase, r0, valid, scale_log2); break;
+            case 4: tile_n<4>(kbase, r0, valid, scale_log2); break;
+            case 5: tile_n<5>(kbase, r0, valid, scale_log2); break;
+            case 6: tile_n<6>(kbase, r0, valid, scale_log2); break;
+            case 7: tile_n<7>(kbase, r0, valid, scale_log2); break;
+            default: if (nh > 0) tile_n<GT>(kbase, r0, valid, scale_log2); break;
+        }
+    }
+
+    template <int NH>
+    __device__ __forceinline__ void tile_n(uint32_t kbase, int r0, int valid, float scale_log2) {
         const uint32_t vbase = kbase + HALF;
         const int t = lane % T;
         const int half = lane / T;
-        float x[GT];
+        float x[NH];
 #pragma unroll
-        for (int g = 0; g < GT; ++g) x[g] = 0.f;
+        for (int g = 0; g < NH; ++g) x[g] = 0.f;
 #pragma unroll 4
         for (int c = 0; c < CHUNKS; ++c) {
             const int chunk = half * CHUNKS + c;
             const float4 kv = lds_f4(kbase + swz128<ROWS>(r0 + t, chunk));
 #pragma unroll
-            for (int g = 0; g < GT; ++g) {
-                if (g < nh) {
-                    const float4 qv = lds_f4(qs + (g * D + chunk * 4) * 4);
-                    x[g] = fmaf(qv.x, kv.x, x[g]);
-                    x[g] = fmaf(qv.y, kv.y, x[g]);
-                    x[g] = fmaf(qv.z, kv.z, x[g]);
-                    x[g] = fmaf(qv.w, kv.w, x[g]);
-                }
+            for (int g = 0; g < NH; ++g) {
+                const float4 qv = lds_f4(qs + (g * D + chunk * 4) * 4);
+                x[g] = fmaf(qv.x, kv.x, x[g]);
+                x[g] = fmaf(qv.y, kv.y, x[g]);
+                x[g] = fmaf(qv.z, kv.z, x[g]);
+                x[g] = fmaf(qv.w, kv.w, x[g]);
             }
         }
 #pragma unroll
-        for (int g = 0; g < GT; ++g) {
-            if (g < nh) {
-                float s = x[g];
-                if (HALVES == 2) s += __shfl_xor_sync(kFullMask, s, 16);
-                s = t < valid ? s * scale_log2 : -INFINITY;
-                float mx = s;
+        for (int g = 0; g < NH; ++g) {
+            float s = x[g];
+            if (HALVES == 2) s += __shfl_xor_sync(kFullMask, s, 16);
+            s = t < valid ? s * scale_log2 : -INFINITY;
+            float mx = s;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
-                const float nm = fmaxf(m[g], mx);
-                const float u = nm == -INFINITY ? 0.f : nm;
-                const float alpha = exp2f(m[g] - u);
-                m[g] = nm;
-                const float p = exp2f(s - u);
-                l[g] = l[g] * alpha + (half == 0 ? p : 0.f);
+            for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
+            const float nm = fmaxf(m[g], mx);
+            const float u = nm == -INFINITY ? 0.f : nm;
+            const float alpha = exp2f(m[g] - u);
+            m[g] = nm;
+            const float p = exp2f(s - u);
+            l[g] = l[g] * alpha + (half == 0 ? p : 0.f);
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[g][i] *= alpha;
-                x[g] = p;
-            }
+            for (int i = 0; i < DPL; ++i) acc[g][i] *= alpha;
+            x[g] = p;
         }
-#pragma unroll 4
+#pragma unroll 8
         for (int tt = 0; tt < T; ++tt) {
             float vv[DPL];
             if constexpr (DPL == 2) {
@@ -376,12 +388,10 @@ struct FloatEngine {
                 vv[3] = v4.w;
             }
 #pragma unroll
-            for (int g = 0; g < GT; ++g) {
-                if (g < nh) {
-                    const float p = __shfl_sync(kFullMask, x[g], tt);
+            for (int g = 0; g < NH; ++g) {
+                const float p = __shfl_sync(kFullMask, x[g], tt);
 #pragma unroll
-                    for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
-                }
+                for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
             }
         }
     }

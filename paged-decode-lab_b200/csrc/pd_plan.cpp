@@ -23,9 +23,11 @@ namespace pd {
 
 namespace {
 thread_local std::string g_last_error;
-// Page tiles (K + V of HG heads) aim at this size: four TMA boxes of up to
-// 16 KiB each keep the single issuing thread far ahead of HBM (a TMA
-// instruction costs about the same to issue whatever its size).
+// FP16 page tiles (K + V of HG heads) aim at this size: four TMA boxes of up
+// to 16 KiB each keep the single issuing thread far ahead of HBM (a TMA
+// instruction costs about the same to issue whatever its size).  FP32 tiles
+// aim at half of it: FP32 warps fold tiles more slowly, so more ring slots
+// per sub-pipeline matter more than fewer TMA instructions.
 constexpr int kTileTargetBytes = 64 * 1024;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -114,7 +116,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // its page tiles carry HG heads' K and V for one page.
     const int T = L.page_size;
     // PD_TILE_KIB overrides the tile target (tuning; capped at 64 KiB).
-    int target = kTileTargetBytes;
+    int target = dtype == PD_FLOAT16 ? kTileTargetBytes : kTileTargetBytes / 2;
     if (const char *env = std::getenv("PD_TILE_KIB")) {
         const int kib = std::atoi(env);
         if (kib >= 1) target = kib * 1024;

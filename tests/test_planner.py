@@ -136,8 +136,8 @@ def test_plan_errors_mirror_reference_messages():
 @pytest.mark.parametrize("dim,page,kv_heads,dtype,expected", [
     (128, 16, 8, "float16", 8), (128, 32, 8, "float16", 4), (64, 16, 8, "float16", 8),
     (64, 32, 32, "float16", 8), (128, 32, 1, "float16", 1), (128, 16, 6, "float16", 2),
-    (128, 16, 8, "float32", 4), (64, 32, 32, "float32", 4), (128, 32, 8, "float32", 2)])
-def test_heads_per_tile_targets_64kib_tiles(dim, page, kv_heads, dtype, expected):
+    (128, 16, 8, "float32", 2), (64, 32, 32, "float32", 2), (128, 32, 8, "float32", 1)])
+def test_heads_per_tile_targets_64kib_fp16_32kib_fp32_tiles(dim, page, kv_heads, dtype, expected):
     layout = Layout(2, kv_heads * 4, kv_heads, dim, page, 8)
     plan = inspect_plan(layout, np.arange(8, dtype=np.int32).reshape(2, 4), [page * 4, 1], num_ctas=3,
                         dtype=dtype)

@@ -60,25 +60,29 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// K or V cache [P, T, Hkv, D] viewed as 4-D {D, T, Hkv, P} (strides in bytes:
-// elt, Hkv*D*elt, D*elt, T*Hkv*D*elt).  One box = 128 bytes of head dims x
-// all T tokens x HG KV heads of one page, landing in shared memory as
-// [head][token] rows of 128 bytes, so the 128-byte swizzle XORs by token.
+// K or V cache [P, T, Hkv, D] viewed as 5-D {128/elt, T, D*elt/128, Hkv, P}
+// (strides in bytes: elt, Hkv*D*elt, 128, D*elt, T*Hkv*D*elt).  One box = all
+// of a page's rows for HG KV heads, landing in shared memory as
+// [head][128-byte box of the row][token] rows of 128 bytes, so the 128-byte
+// swizzle XORs by token and one instruction moves the whole K (or V) page.
 pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, int hg, CUtensorMap *map) {
     auto encode = tensor_map_encoder();
     if (!encode) return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t elt = dtype == PD_FLOAT16 ? 2 : 4;
     const pd_layout &L = p.layout;
     const cuuint64_t row = cuuint64_t(L.head_dim) * elt;
-    cuuint64_t dims[4] = {cuuint64_t(L.head_dim), cuuint64_t(L.page_size), cuuint64_t(L.kv_heads),
+    // {128 bytes of a row, token, 128-byte box of the row, KV head, page}: one
+    // box {all, T, all, hg, 1} lands as [head][box][token] 128-byte rows.
+    const cuuint64_t nbox = row / 128;
+    cuuint64_t dims[5] = {128 / elt, cuuint64_t(L.page_size), nbox, cuuint64_t(L.kv_heads),
                           cuuint64_t(L.physical_pages)};
-    cuuint64_t strides[3] = {row * cuuint64_t(L.kv_heads), row, row * cuuint64_t(L.kv_heads) * L.page_size};
-    cuuint32_t box[4] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(hg), 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
+    cuuint64_t strides[4] = {row * cuuint64_t(L.kv_heads), 128, row, row * cuuint64_t(L.kv_heads) * L.page_size};
+    cuuint32_t box[5] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(nbox), cuuint32_t(hg), 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = encode(map,
                               dtype == PD_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                              4, const_cast<void *>(base), dims, strides, box, estr,
+                              5, const_cast<void *>(base), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)

@@ -8,12 +8,13 @@
 //     query-head tile); the host balances page tiles across CTAs, so every SM
 //     streams the same number of bytes, ragged batches included;
 //   * warp NC (producer) looks up each page in the page table and gathers the
-//     page's K and V rows for all HG KV heads of the group with 4-D tiled TMA
-//     loads ({D, T, Hkv, P} view, 128-byte swizzle, no multicast) into a ring
-//     of shared-memory slots, completion tracked by mbarriers.  Boxes cover
-//     HG heads at once because a TMA instruction costs the same ~75 issue
-//     cycles whatever its size; many bytes per instruction keep one thread
-//     ahead of HBM;
+//     page's K rows, then its V rows, for all HG KV heads of the group with
+//     one 5-D tiled TMA load each ({128 B of a row, T, D*elt/128, Hkv, P}
+//     view, 128-byte swizzle, no multicast) into a ring of shared-memory
+//     slots, completion tracked by mbarriers.  One instruction moves a whole
+//     K or V page of HG heads because a TMA instruction costs the same ~75
+//     issue cycles whatever its size; many bytes per instruction keep one
+//     thread ahead of HBM;
 //   * a consumer warp owns one KV head of the group and a slice of 8 of its
 //     query heads (QT = GT / 8 slices; wide groups such as MQA split their
 //     query heads over warps that read the same tile) and takes every NSUB-th
@@ -69,8 +70,8 @@ struct KernelShape {
     static constexpr int ROW_BYTES = D * ELT;
     static constexpr int NBOX = ROW_BYTES / 128;       // 128-byte TMA boxes per token row
     static constexpr int BOX_ELEMS = 128 / ELT;
-    static constexpr int ROWS = HG * T;                // swizzle rows per box: [head][token]
-    static constexpr int HALF_BYTES = NBOX * ROWS * 128;  // K (or V) part of one page tile
+    static constexpr int HEAD_BYTES = NBOX * T * 128;  // one head's K (or V) rows: [box][token]
+    static constexpr int HALF_BYTES = HG * HEAD_BYTES; // K (or V) part of one page tile: [head][box][token]
     static constexpr int TILE_BYTES = 2 * HALF_BYTES;
     static constexpr int THREADS = (NC + 1) * 32;
     static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
@@ -93,14 +94,14 @@ struct SmemFlags {
 // S^T[t][g] = K[t][:] . Q[g][:]  with A = K tile (ldmatrix), B = Q^T fragments;
 // O^T[d][g] += V^T[d][t] P^T[t][g] with A = V tile (ldmatrix.trans), B = P^T,
 // where P^T comes from the S^T accumulators by movmatrix.trans (no shared memory).
-// Tile rows are [head][token] 128-byte rows; this warp's head starts at row r0.
-template <int D, int T, int GT, int ROWS>
+// A head's K (or V) rows sit in NBOX boxes of T 128-byte rows each: byte
+// box*T*128 + t*128 of the head's block, 16-byte chunks XORed by t % 8.
+template <int D, int T, int GT>
 struct HalfEngine {
     static constexpr int NT = GT / 8;    // n-tiles of 8 query heads
     static constexpr int KS = D / 16;    // k-steps of the QK^T product
     static constexpr int DT = D / 16;    // m-tiles of the PV product (head dims)
     static constexpr int MT = T / 16;    // 16-token m-tiles per page
-    static constexpr int HALF = (D * 2 / 128) * ROWS * 128;
     static constexpr bool Q_REGS = NT <= 2;
 
     uint32_t qf[Q_REGS ? KS : 1][Q_REGS ? NT : 1][2];
@@ -163,8 +164,7 @@ struct HalfEngine {
         }
     }
 
-    __device__ __forceinline__ void tile(uint32_t kbase, int r0, int valid, float scale_log2) {
-        const uint32_t vbase = kbase + HALF;
+    __device__ __forceinline__ void tile(uint32_t kbase, uint32_t vbase, int valid, float scale_log2) {
         const int mi = lane >> 3, r8 = lane & 7;
         float x[MT][NT][4];
 #pragma unroll
@@ -173,11 +173,11 @@ struct HalfEngine {
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) x[mt][nt][i] = 0.f;
-            const int row = r0 + mt * 16 + r8 + (mi & 1) * 8;
+            const int row = mt * 16 + r8 + (mi & 1) * 8;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 uint32_t a[4];
-                ldmatrix_x4(a, kbase + swz128<ROWS>(row, ks * 2 + (mi >> 1)));
+                ldmatrix_x4(a, kbase + swz128<T>(row, ks * 2 + (mi >> 1)));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     uint32_t b0, b1;
@@ -242,11 +242,11 @@ struct HalfEngine {
         }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-            const int row = r0 + mt * 16 + r8 + (mi >> 1) * 8;
+            const int row = mt * 16 + r8 + (mi >> 1) * 8;
 #pragma unroll
             for (int dt = 0; dt < DT; ++dt) {
                 uint32_t a[4];
-                ldmatrix_x4_trans(a, vbase + swz128<ROWS>(row, dt * 2 + (mi & 1)));
+                ldmatrix_x4_trans(a, vbase + swz128<T>(row, dt * 2 + (mi & 1)));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_16816(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
             }
@@ -294,12 +294,11 @@ struct HalfEngine {
 // ------------------------------------------------------------------ FP32 engine
 // Lanes own tokens for the scores (one row of K per lane, Q broadcast from
 // shared memory) and own head dims for the value sum.
-template <int D, int T, int GT, int ROWS>
+template <int D, int T, int GT>
 struct FloatEngine {
     static constexpr int DPL = D / 32;             // value dims per lane
     static constexpr int HALVES = 32 / T;          // lanes per token in the score phase
     static constexpr int CHUNKS = D / 4 / HALVES;  // float4 chunks of K per lane
-    static constexpr int HALF = (D * 4 / 128) * ROWS * 128;
 
     float acc[GT][DPL];
     float m[GT], l[GT];
@@ -321,22 +320,21 @@ struct FloatEngine {
 
     // The head count is dispatched to a compile-time bound so that an MHA
     // warp (one query head) runs no code for the seven unused head slots.
-    __device__ __forceinline__ void tile(uint32_t kbase, int r0, int valid, float scale_log2) {
+    __device__ __forceinline__ void tile(uint32_t kbase, uint32_t vbase, int valid, float scale_log2) {
         switch (nh) {
-            case 1: tile_n<1>(kbase, r0, valid, scale_log2); break;
-            case 2: tile_n<2>(kbase, r0, valid, scale_log2); break;
-            case 3: tile_n<3>(kbase, r0, valid, scale_log2); break;
-            case 4: tile_n<4>(kbase, r0, valid, scale_log2); break;
-            case 5: tile_n<5>(kbase, r0, valid, scale_log2); break;
-            case 6: tile_n<6>(kbase, r0, valid, scale_log2); break;
-            case 7: tile_n<7>(kbase, r0, valid, scale_log2); break;
-            default: if (nh > 0) tile_n<GT>(kbase, r0, valid, scale_log2); break;
+            case 1: tile_n<1>(kbase, vbase, valid, scale_log2); break;
+            case 2: tile_n<2>(kbase, vbase, valid, scale_log2); break;
+            case 3: tile_n<3>(kbase, vbase, valid, scale_log2); break;
+            case 4: tile_n<4>(kbase, vbase, valid, scale_log2); break;
+            case 5: tile_n<5>(kbase, vbase, valid, scale_log2); break;
+            case 6: tile_n<6>(kbase, vbase, valid, scale_log2); break;
+            case 7: tile_n<7>(kbase, vbase, valid, scale_log2); break;
+            default: if (nh > 0) tile_n<GT>(kbase, vbase, valid, scale_log2); break;
         }
     }
 
     template <int NH>
-    __device__ __forceinline__ void tile_n(uint32_t kbase, int r0, int valid, float scale_log2) {
-        const uint32_t vbase = kbase + HALF;
+    __device__ __forceinline__ void tile_n(uint32_t kbase, uint32_t vbase, int valid, float scale_log2) {
         const int t = lane % T;
         const int half = lane / T;
         float x[NH];
@@ -345,7 +343,7 @@ struct FloatEngine {
 #pragma unroll 4
         for (int c = 0; c < CHUNKS; ++c) {
             const int chunk = half * CHUNKS + c;
-            const float4 kv = lds_f4(kbase + swz128<ROWS>(r0 + t, chunk));
+            const float4 kv = lds_f4(kbase + swz128<T>(t, chunk));
 #pragma unroll
             for (int g = 0; g < NH; ++g) {
                 const float4 qv = lds_f4(qs + (g * D + chunk * 4) * 4);
@@ -377,11 +375,11 @@ struct FloatEngine {
         for (int tt = 0; tt < T; ++tt) {
             float vv[DPL];
             if constexpr (DPL == 2) {
-                const float2 v2 = lds_f2(vbase + swz128<ROWS>(r0 + tt, lane >> 1) + (lane & 1) * 8);
+                const float2 v2 = lds_f2(vbase + swz128<T>(tt, lane >> 1) + (lane & 1) * 8);
                 vv[0] = v2.x;
                 vv[1] = v2.y;
             } else {
-                const float4 v4 = lds_f4(vbase + swz128<ROWS>(r0 + tt, lane));
+                const float4 v4 = lds_f4(vbase + swz128<T>(tt, lane));
                 vv[0] = v4.x;
                 vv[1] = v4.y;
                 vv[2] = v4.z;
@@ -421,15 +419,15 @@ struct FloatEngine {
     }
 };
 
-template <typename Elt, int D, int T, int GT, int ROWS>
+template <typename Elt, int D, int T, int GT>
 struct EngineFor;
-template <int D, int T, int GT, int ROWS>
-struct EngineFor<__half, D, T, GT, ROWS> {
-    using type = HalfEngine<D, T, GT, ROWS>;
+template <int D, int T, int GT>
+struct EngineFor<__half, D, T, GT> {
+    using type = HalfEngine<D, T, GT>;
 };
-template <int D, int T, int GT, int ROWS>
-struct EngineFor<float, D, T, GT, ROWS> {
-    using type = FloatEngine<D, T, GT, ROWS>;
+template <int D, int T, int GT>
+struct EngineFor<float, D, T, GT> {
+    using type = FloatEngine<D, T, GT>;
 };
 
 // ------------------------------------------------------------------ kernel
@@ -442,7 +440,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     using S = KernelShape<Elt, D, T, GT, HG, NSUB, SLOTS>;
     constexpr int NC = S::NC;
     static_assert(S::ROW_BYTES % 128 == 0, "token rows must be whole 128-byte boxes");
-    static_assert((S::ROWS * 128) % 1024 == 0, "boxes must keep 1024-byte swizzle alignment");
+    static_assert(T % 8 == 0, "boxes of T rows must keep 1024-byte swizzle alignment");
     static_assert(S::SMEM <= 232448, "shared memory budget exceeded");
     // Tile j goes to slot j % SLOTS and to the warps of sub-pipeline j % NSUB;
     // with SLOTS a multiple of NSUB every slot is consumed by one fixed set of
@@ -505,13 +503,9 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                             slot_valid[slot] = 1;
                             mbar_arrive_expect_tx(fb, S::TILE_BYTES);
                             const uint32_t dst = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
-#pragma unroll
-                            for (int bx = 0; bx < S::NBOX; ++bx)
-                                tma_load_4d(dst + bx * S::ROWS * 128, &tm_k, bx * S::BOX_ELEMS, 0, kv0, page, fb);
-#pragma unroll
-                            for (int bx = 0; bx < S::NBOX; ++bx)
-                                tma_load_4d(dst + S::HALF_BYTES + bx * S::ROWS * 128, &tm_v, bx * S::BOX_ELEMS,
-                                            0, kv0, page, fb);
+                            // one instruction each for all of the page's K and V rows
+                            tma_load_5d(dst, &tm_k, 0, 0, 0, kv0, page, fb);
+                            tma_load_5d(dst + S::HALF_BYTES, &tm_v, 0, 0, 0, kv0, page, fb);
                         } else {
                             // The reference skips tokens whose page id is out of range
                             // (decode.cu:58); plans validate ids, so this is defence only.
@@ -530,7 +524,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     const int hh = warp % S::CPT / S::QT;   // KV head of the group this warp owns
     const int qt = warp % S::QT;            // its 8-query-head slice of that head
     const int sub = warp / S::CPT;          // it takes tiles j with j % NSUB == sub
-    const int r0 = hh * T;          // its rows in a [head][token] tile
+    const int hoff = hh * S::HEAD_BYTES;   // its head's block in each half of a tile
     bool stop = false;
     int j = 0;
     for (int si = seg_begin; si < seg_end; ++si) {
@@ -557,12 +551,12 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                 const int lp = sg.y + t;
                 const int valid = min(T, length - lp * T);
                 if (slot_valid[slot]) {
-                    const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+                    const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES) + hoff;
                     const int64_t base = (int64_t(b) * a.Hkv + kv0 + hh) * a.max_len + int64_t(lp) * T;
                     for (int idx = lane; idx < valid * CPR; idx += 32) {
                         const int r = idx / CPR, c = idx % CPR;
-                        const float4 kv = lds_f4(kb + swz128<S::ROWS>(r0 + r, c));
-                        const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<S::ROWS>(r0 + r, c));
+                        const float4 kv = lds_f4(kb + swz128<T>(r, c));
+                        const float4 vv = lds_f4(kb + S::HALF_BYTES + swz128<T>(r, c));
                         const int64_t off = (base + r) * S::ROW_BYTES + c * 16;
                         *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_k) + off) = kv;
                         *reinterpret_cast<float4 *>(static_cast<uint8_t *>(a.dense_v) + off) = vv;
@@ -573,7 +567,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             }
             j += npg;
         } else {
-            using Engine = typename EngineFor<Elt, D, T, 8, S::ROWS>::type;
+            using Engine = typename EngineFor<Elt, D, T, 8>::type;
             Engine eng;
             // this warp's query heads: (kv0 + hh) * G + qoff + qt * 8 + g, g < nw
             const int nw = min(8, nh - qt * 8);     // may be <= 0: the warp then idles on its tiles
@@ -581,7 +575,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             const Elt *qrow = static_cast<const Elt *>(a.q) + qhead0 * D;
             uint8_t *qmine = qsm + size_t(warp) * 8 * D * sizeof(Elt);
             const uint32_t qs = smem_u32(qmine);
-            static_assert(!std::is_same<Elt, __half>::value || HalfEngine<D, T, 8, S::ROWS>::Q_REGS,
+            static_assert(!std::is_same<Elt, __half>::value || HalfEngine<D, T, 8>::Q_REGS,
                           "FP16 warps keep their 8 query heads in registers");
             if constexpr (S::Q_SMEM) {
                 // this warp's Q rows (zero rows for heads past nh) into its own slice
@@ -613,7 +607,8 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                 }
                 if (slot_valid[slot]) {
                     const int lp = sg.y + t;
-                    eng.tile(smem_u32(ring + size_t(slot) * S::TILE_BYTES), r0, min(T, length - lp * T),
+                    const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES) + hoff;
+                    eng.tile(kb, kb + S::HALF_BYTES, min(T, length - lp * T),
                              a.scale_log2);
                 }
                 __syncwarp();

@@ -80,13 +80,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-// 4-D tiled load into CTA shared memory, completion counted on `bar`.
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
-                                            int c3, uint32_t bar) {
+// 5-D tiled load into CTA shared memory, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            int c3, int c4, uint32_t bar) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
         : "memory");
 }
 
@@ -154,9 +154,9 @@ __device__ __forceinline__ float2 lds_f2(uint32_t addr) {
 }
 
 // Offset of the 16-byte chunk `chunk` (counted along the row) of row `row`
-// inside a tile written by TMA with CU_TENSOR_MAP_SWIZZLE_128B: each box is
-// rows x 128 B, and inside every 8-row / 1024-byte atom the chunk index is
-// XORed with (row % 8).  Tiles are 1024-byte aligned.
+// inside a block written by TMA with CU_TENSOR_MAP_SWIZZLE_128B: each 128-byte
+// box of the row is ROWS rows x 128 B, and inside every 8-row / 1024-byte atom
+// the chunk index is XORed with (row % 8).  Blocks are 1024-byte aligned.
 template <int ROWS>
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
     const int box = chunk >> 3;

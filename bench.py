@@ -349,7 +349,10 @@ def run_ours(args, rank, local, world):
         step()
     barrier(world)
 
-    # (1) K back-to-back steps, bracketed; each launch also has its own events
+    # (1) K steps.  Inputs larger than L2 run back to back between one pair of
+    # events (events between the steps would add their own gaps); smaller
+    # inputs flush L2 before every step, and each step then has its own events
+    # so that the flushes stay outside the timed time.
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -359,19 +362,22 @@ def run_ours(args, rank, local, world):
     for i in range(args.steps):
         if flush is not None:
             flush.amax()
-        starts[i].record(stream)
+            starts[i].record(stream)
         step()
-        ends[i].record(stream)
+        if flush is not None:
+            ends[i].record(stream)
     t_end.record(stream)
     barrier(world)
     clocks.mark_end()
     clocks.stop()
-    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = t_start.elapsed_time(t_end)
-    if flush is not None:            # flushes sit between steps: count decode time only
+    if flush is not None:
+        launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         total_ms = sum(launch_ms)
+    else:
+        total_ms = t_start.elapsed_time(t_end)
     step_ms = max_over_ranks(total_ms / args.steps, world)
-    kernel_ms = statistics.mean(launch_ms)
+    # the step's kernels (decode, plus the merge kernel when it is separate) per launch
+    kernel_ms = total_ms / args.steps
     errors = job.decode_plan.read_errors()
     if errors:
         raise SystemExit(f"device error word {errors:#x}")
@@ -467,7 +473,9 @@ def run_ours(args, rank, local, world):
                    "kv_heads_per_tile": int(info.heads_per_tile)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "kernel": "paged_decode_kernel (+ merge_partials_kernel)",
+                     "traffic": traffic,
+                     "kernel": "paged_decode_kernel" + ("" if job.kernels_per_step() == 1
+                                                        else " (+ merge_partials_kernel)"),
                      "kernel_us": kernel_ms * 1e3,
                      "algorithmic_bytes_per_launch": job.bytes_rank},
         "gpu_launches": args.steps * job.kernels_per_step(),

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 1
+#define PD_ABI_VERSION 2
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -75,6 +75,9 @@ typedef struct pd_plan_info {
     int32_t group_tile;      /* query heads per group tile (8, 16 or 32) */
     int32_t heads_per_tile;  /* KV heads gathered per page tile (1, 2, 4 or 8) */
     int32_t total_pages;     /* page tiles streamed per decode (all groups) */
+    int32_t merge_rows;      /* output rows merged from partials after the decode */
+    int32_t merge_in_kernel; /* 1: the decode CTAs merge them after a grid barrier (cooperative
+                                launch; num_ctas <= SMs), 0: a dependent merge kernel does */
     int64_t workspace_bytes; /* split-K partials + merge counters */
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
 } pd_plan_info;
@@ -83,8 +86,9 @@ typedef struct pd_plan_info {
  * split planning (runtime.py:32-69) and decode_cuda's validation
  * (decode.cu:201-237).  Copies table and lengths.  merge_mode 0 = "serial",
  * 1 = "shared" is accepted for API compatibility (runtime.py:33-34); the
- * decode always merges split partials the same way (a dependent merge kernel
- * launched right behind the decode kernel).  A plan serves one input dtype:
+ * decode always merges split partials the same way (the decode CTAs after a
+ * grid barrier when num_ctas <= SMs, else a dependent merge kernel launched
+ * right behind the decode kernel).  A plan serves one input dtype:
  * the page tiles it gathers are sized for it (the Python DecodePlan keeps one
  * plan per dtype behind its dtype-agnostic run()).  device < 0 builds a
  * host-only plan (inspection, no decode).  num_ctas <= 0 picks one CTA per SM
@@ -122,8 +126,10 @@ pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *s
 /* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
  * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
  * k and v must be 16-byte aligned (TMA); dtype must be the plan's.
- * Asynchronous on `stream`: one decode kernel, plus a merge kernel when the
- * plan has partial slots.
+ * Asynchronous on `stream`: one decode kernel (a cooperative launch that
+ * also merges the partials when the plan has some and num_ctas <= SMs), or
+ * the decode kernel and a dependent merge kernel.  Launches of one plan must
+ * stay in one stream order: they share the plan's partial slots and barrier.
  */
 pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
                     float *out, void *stream);

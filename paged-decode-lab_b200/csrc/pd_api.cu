@@ -121,7 +121,7 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     const DeviceImage &im = p->image;
     a.q = q;
     a.table = reinterpret_cast<const int32_t *>(dev + im.off_table);
-    a.cta_off = reinterpret_cast<const int32_t *>(dev + im.off_cta);
+    a.head = reinterpret_cast<const int4 *>(dev + im.off_head);
     a.segs = reinterpret_cast<const int4 *>(dev + im.off_segs);
     a.groups = reinterpret_cast<const int4 *>(dev + im.off_groups);
     a.part_o = reinterpret_cast<float *>(dev + im.off_part_o);
@@ -136,6 +136,10 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.group = p->group;
     a.slot_stride = p->slot_stride;
     a.num_groups = int32_t(p->groups.size() / 8);
+    a.ticket = reinterpret_cast<unsigned long long *>(dev + im.off_error + 8);
+    a.merge_rows = reinterpret_cast<const int4 *>(dev + im.off_merge);
+    a.num_merge_rows = int32_t(p->merge_rows.size() / 4);
+    a.fused_merge = p->merge_in_kernel ? 1 : 0;
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
@@ -165,12 +169,40 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     pd_status s = ensure_smem_attribute(p->device, e);
     if (s != PD_OK) return s;
     const auto st = static_cast<cudaStream_t>(stream);
-    e.fn<<<p->num_ctas, e.threads, e.smem, st>>>(tc.map_k, tc.map_v, args);
-    cudaError_t err = cudaGetLastError();
+    DecodeArgs la = args;
+    if (mode != kModeDecode) la.fused_merge = 0;
+    // Every decode launch is programmatically dependent on the kernel before
+    // it (the kernel waits with griddepcontrol.wait before touching q, the
+    // caches or its outputs), so its launch and set-up overlap that kernel.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(p->num_ctas));
+    cfg.blockDim = dim3(unsigned(e.threads));
+    cfg.dynamicSmemBytes = e.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.attrs = attr;
+    cudaError_t err;
+    if (la.fused_merge) {
+        // The CTAs wait for each other at a grid barrier before merging; a
+        // cooperative launch guarantees they are all resident, or refuses.
+        cfg.numAttrs = 2;
+        err = cudaLaunchKernelEx(&cfg, e.fn, tc.map_k, tc.map_v, la);
+        if (err == cudaSuccess) return PD_OK;
+        if (err != cudaErrorCooperativeLaunchTooLarge)
+            return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
+        (void)cudaGetLastError();   // not all CTAs fit at once: merge with the separate kernel
+        la.fused_merge = 0;
+    }
+    cfg.numAttrs = 1;
+    err = cudaLaunchKernelEx(&cfg, e.fn, tc.map_k, tc.map_v, la);
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
     if (mode == kModeDecode && p->num_pieces > 0) {
-        err = launch_merge_partials(args, p->heads_per_tile, p->group_tile, e.nsub, p->layout.head_dim, st);
+        err = launch_merge_partials(la, p->heads_per_tile, p->group_tile, e.nsub, p->layout.head_dim, st);
         if (err != cudaSuccess)
             return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
     }
@@ -237,6 +269,8 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->heads_per_tile = p->heads_per_tile;
     info->slot_stride = p->slot_stride;
     info->total_pages = int32_t(p->total_pages);
+    info->merge_rows = int32_t(p->merge_rows.size() / 4);
+    info->merge_in_kernel = p->merge_in_kernel ? 1 : 0;
     info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o);
     info->device_bytes = int64_t(p->image.bytes);
     return PD_OK;

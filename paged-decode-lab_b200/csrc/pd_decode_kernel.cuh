@@ -41,7 +41,8 @@ namespace pd {
 struct DecodeArgs {
     const void *q;            // [B, Hq, D] in the input dtype
     const int32_t *table;     // [B, W]
-    const int32_t *cta_off;   // [C + 1] segment range of each CTA
+    const int4 *head;         // [C][16] per-CTA header: {seg_begin, seg_end}, first segment,
+                              // its group (2 int4), page ids of its first 32 pages
     const int4 *segs;         // {group, first_page, end_page, slot (-1: write output directly)}
     const int4 *groups;       // 2 per group: {b, kv_head0, q_head_offset, nh}, {length, slot0, segments, 0}
     float *part_o;            // [slots, HG, GT, D] unnormalised partial outputs
@@ -54,6 +55,11 @@ struct DecodeArgs {
     int32_t Hq, Hkv, W, max_len, group;   // group = G = Hq / Hkv
     int32_t slot_stride;      // partial slots reserved per segment (>= NSUB)
     int32_t num_groups;
+    // in-kernel merge (cooperative launch): grid barrier ticket and the rows to merge
+    unsigned long long *ticket;
+    const int4 *merge_rows;      // split groups' rows: {out row, slot0, segments, head * GT + query head}
+    int32_t num_merge_rows;
+    int32_t fused_merge;         // 1: the CTAs merge the partials after a grid barrier
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
 };
@@ -433,6 +439,145 @@ struct EngineFor<float, D, T, GT> {
 // ------------------------------------------------------------------ kernel
 enum : int { kModeDecode = 0, kModeGather = 1 };
 
+// ------------------------------------------------------------------ in-kernel merge
+// Runs in every CTA after the grid barrier of a cooperative launch, in place
+// of the separate merge kernel.  The split groups' output rows (merge_rows,
+// {out row, first slot, segments, column}) are cut into gridDim.x contiguous
+// shares.  With at least NC rows a warp takes every NC-th row of its CTA's
+// share and merges it alone; with fewer, each row gets a team of NC / rows
+// warps whose states meet in shared memory (`scratch`, the idle ring) and are
+// combined by the row's first warp in member order.  A warp folds its
+// partials into a running (m, l, o) with the max-corrected merge (the
+// oracle.py:88-96 algebra), U partials in flight per lane, so a row costs one
+// or two L2 round trips.  Every launch adds the same numbers in the same
+// order.  Partials are read at L2 (ld.global.cg): other SMs wrote them during
+// this launch.
+template <int D, int HG, int GT, int NSUB>
+struct RowMerge {
+    static constexpr int CH = D / 4;                  // float4 chunks of a row
+    static constexpr int LP = CH < 32 ? 32 / CH : 1;  // lane groups, each on its own partials
+    static constexpr int CPL = CH > 32 ? CH / 32 : 1; // chunks per lane
+    static constexpr int U = 8;
+    float m, l;
+    float4 o[CPL];
+
+    __device__ __forceinline__ void add(float om, float ol, const float4 (&oo)[CPL]) {
+        if (!(ol > 0.f)) return;
+        const float nm = fmaxf(m, om);
+        const float al = exp2f(m - nm), be = exp2f(om - nm);
+        l = fmaf(l, al, be * ol);
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) {
+            o[cc].x = fmaf(o[cc].x, al, be * oo[cc].x);
+            o[cc].y = fmaf(o[cc].y, al, be * oo[cc].y);
+            o[cc].z = fmaf(o[cc].z, al, be * oo[cc].z);
+            o[cc].w = fmaf(o[cc].w, al, be * oo[cc].w);
+        }
+        m = nm;
+    }
+
+    // Partials first, first + step, ... of the row `meta`; every lane ends with
+    // the merged state of its chunks.
+    __device__ __forceinline__ void fold(const DecodeArgs &a, int4 meta, int first, int step, int lane) {
+        m = -INFINITY;
+        l = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) o[cc] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int lg = LP > 1 ? lane / CH : 0;
+        const int c0 = LP > 1 ? lane % CH : lane;
+        const int parts = meta.z * NSUB;
+        const int st = step * LP;
+        for (int p0 = first + step * lg; p0 < parts; p0 += st * U) {
+            float2 ml[U];
+            float4 ov[U][CPL];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int p = p0 + u * st;
+                ml[u] = make_float2(-INFINITY, 0.f);
+                if (p < parts) {
+                    const int64_t slot = int64_t(meta.y) + int64_t(p / NSUB) * a.slot_stride + p % NSUB;
+                    const int64_t pr = slot * (HG * GT) + meta.w;
+                    ml[u] = __ldcg(a.part_ml + pr);
+                    const float4 *src = reinterpret_cast<const float4 *>(a.part_o + pr * D);
+#pragma unroll
+                    for (int cc = 0; cc < CPL; ++cc) ov[u][cc] = __ldcg(src + c0 + cc * 32);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) add(ml[u].x, ml[u].y, ov[u]);
+        }
+#pragma unroll
+        for (int off = CH; off < 32; off *= 2) {   // fold the lane groups (D < 128)
+            const float om = __shfl_xor_sync(kFullMask, m, off);
+            const float ol = __shfl_xor_sync(kFullMask, l, off);
+            float4 oo[CPL];
+#pragma unroll
+            for (int cc = 0; cc < CPL; ++cc) {
+                oo[cc].x = __shfl_xor_sync(kFullMask, o[cc].x, off);
+                oo[cc].y = __shfl_xor_sync(kFullMask, o[cc].y, off);
+                oo[cc].z = __shfl_xor_sync(kFullMask, o[cc].z, off);
+                oo[cc].w = __shfl_xor_sync(kFullMask, o[cc].w, off);
+            }
+            add(om, ol, oo);
+        }
+    }
+
+    // Normalised output (zero for an empty row) and, if asked, the (m, l) stats.
+    __device__ __forceinline__ void write(const DecodeArgs &a, int4 meta, int lane) const {
+        const int c0 = LP > 1 ? lane % CH : lane;
+        if (LP > 1 && lane >= CH) return;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        float4 *dst = reinterpret_cast<float4 *>(a.out + int64_t(meta.x) * D);
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc)
+            dst[c0 + cc * 32] = make_float4(o[cc].x * inv, o[cc].y * inv, o[cc].z * inv, o[cc].w * inv);
+        if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[meta.x] = make_float2(m, l);
+    }
+};
+
+template <int D, int HG, int GT, int NSUB, int NC>
+__device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *scratch, int warp, int lane,
+                                                int64_t lo, int rows, int team, int4 meta0) {
+    using M = RowMerge<D, HG, GT, NSUB>;
+    M rm;
+    if (team == 1) {
+        int4 meta = meta0;
+        for (int r = warp; r < rows; r += NC) {
+            const int4 next = r + NC < rows ? __ldg(a.merge_rows + lo + r + NC) : meta;
+            rm.fold(a, meta, 0, 1, lane);
+            rm.write(a, meta, lane);
+            meta = next;
+        }
+        return;
+    }
+    float4 *res_o = reinterpret_cast<float4 *>(scratch);                         // [NC][D / 4]
+    float2 *res_ml = reinterpret_cast<float2 *>(scratch + size_t(NC) * D * 4);   // [NC]
+    if (warp < rows * team) {
+        rm.fold(a, meta0, warp / rows, team, lane);
+        const int c0 = M::LP > 1 ? lane % M::CH : lane;
+        if (M::LP == 1 || lane < M::CH) {
+#pragma unroll
+            for (int cc = 0; cc < M::CPL; ++cc) res_o[warp * M::CH + c0 + cc * 32] = rm.o[cc];
+        }
+        if (lane == 0) res_ml[warp] = make_float2(rm.m, rm.l);
+    }
+    named_barrier_sync(1, NC * 32);
+    if (warp < rows) {
+        // member 0 of row `warp` combines members k = 1 .. team - 1 (warps warp + k * rows)
+        const int c0 = M::LP > 1 ? lane % M::CH : lane;
+        for (int k = 1; k < team; ++k) {
+            const float2 ml = res_ml[warp + k * rows];
+            float4 oo[M::CPL];
+#pragma unroll
+            for (int cc = 0; cc < M::CPL; ++cc)
+                oo[cc] = (M::LP == 1 || lane < M::CH) ? res_o[(warp + k * rows) * M::CH + c0 + cc * 32]
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            rm.add(ml.x, ml.y, oo);
+        }
+        rm.write(a, meta0, lane);
+    }
+}
+
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS, int MODE>
 __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -459,8 +604,11 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int seg_begin = a.cta_off[blockIdx.x];
-    const int seg_end = a.cta_off[blockIdx.x + 1];
+    // Every warp reads the CTA header (12 int4, one per lane): the first page
+    // tile then needs one dependent load before its TMA instead of four.
+    const int4 hv = lane < 12 ? __ldg(a.head + int64_t(blockIdx.x) * 16 + lane) : make_int4(0, 0, 0, 0);
+    const int seg_begin = __shfl_sync(kFullMask, hv.x, 0);
+    const int seg_end = __shfl_sync(kFullMask, hv.y, 0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SLOTS; ++s) {
@@ -471,6 +619,10 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         mbar_init_fence();
     }
     __syncthreads();
+    // Launched programmatically dependent on the previous kernel in the
+    // stream: everything above (plan metadata, shared-memory set-up) may
+    // overlap its tail; q, the caches and every output wait for it to finish.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == NC) {
         // ------------------------------------------------------------ producer
@@ -480,14 +632,22 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         }
         bool stop = false;
         int j = 0;
+        int4 sg = shfl_int4(hv, 1), g0 = shfl_int4(hv, 2);
+        // lane i: page id of the first segment's page i (header words 16..47)
+        const int4 hp = shfl_int4(hv, 4 + (lane >> 2));
+        const int first_pages = (lane & 3) == 0 ? hp.x : (lane & 3) == 1 ? hp.y : (lane & 3) == 2 ? hp.z : hp.w;
         for (int si = seg_begin; si < seg_end; ++si) {
-            const int4 sg = a.segs[si];
-            const int4 g0 = a.groups[2 * sg.x];
+            // the next segment and its group load while this one streams
+            const bool more = si + 1 < seg_end;
+            const int4 nsg = more ? __ldg(a.segs + si + 1) : sg;
+            int4 ng0 = g0;
+            bool ng0_loaded = !more;
             const int32_t *trow = a.table + int64_t(g0.x) * a.W;
             const int kv0 = g0.y;
             for (int pg = sg.y; pg < sg.z; pg += 32) {
                 const int n = min(32, sg.z - pg);
-                const int mine = lane < n ? __ldg(trow + pg + lane) : 0;
+                const int mine = (si == seg_begin && pg == sg.y) ? first_pages
+                                                                 : (lane < n ? __ldg(trow + pg + lane) : 0);
                 for (int i = 0; i < n; ++i, ++j) {
                     const int page = __shfl_sync(kFullMask, mine, i);
                     if (lane == 0 && !stop) {
@@ -515,7 +675,14 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                         }
                     }
                 }
+                if (!ng0_loaded) {
+                    ng0 = __ldg(a.groups + 2 * nsg.x);
+                    ng0_loaded = true;
+                }
             }
+            if (!ng0_loaded) ng0 = __ldg(a.groups + 2 * nsg.x);
+            sg = nsg;
+            g0 = ng0;
         }
         return;
     }
@@ -527,10 +694,11 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     const int hoff = hh * S::HEAD_BYTES;   // its head's block in each half of a tile
     bool stop = false;
     int j = 0;
+    const int4 sg_h = shfl_int4(hv, 1), g0_h = shfl_int4(hv, 2), g1_h = shfl_int4(hv, 3);
     for (int si = seg_begin; si < seg_end; ++si) {
-        const int4 sg = a.segs[si];
-        const int4 g0 = a.groups[2 * sg.x];
-        const int4 g1 = a.groups[2 * sg.x + 1];
+        const int4 sg = si == seg_begin ? sg_h : a.segs[si];
+        const int4 g0 = si == seg_begin ? g0_h : a.groups[2 * sg.x];
+        const int4 g1 = si == seg_begin ? g1_h : a.groups[2 * sg.x + 1];
         const int b = g0.x, kv0 = g0.y, qoff = g0.z, nh = g0.w;
         const int length = g1.x;
         const int npg = sg.z - sg.y;
@@ -636,6 +804,29 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                     if (g < nw) a.part_ml[ps * GT + qt * 8 + g] = make_float2(m, l);
                 });
             }
+        }
+    }
+    if constexpr (MODE == kModeDecode) {
+        if (a.fused_merge) {
+            static_assert(size_t(NC) * (D * 4 + 8) <= S::RING, "merge scratch must fit in the ring");
+            // this CTA's share of the merge rows; each warp's first row loads
+            // while the CTAs gather at the barrier
+            const int64_t R = a.num_merge_rows;
+            const int64_t mlo = R * blockIdx.x / gridDim.x;
+            const int mrows = int(R * (blockIdx.x + 1) / gridDim.x - mlo);
+            const int team = (mrows >= NC || mrows == 0) ? 1 : NC / mrows;
+            const bool has = team == 1 ? warp < mrows : warp < mrows * team;
+            const int4 meta0 = has ? __ldg(a.merge_rows + mlo + (team == 1 ? warp : warp % mrows))
+                                   : make_int4(0, 0, 0, 0);
+            named_barrier_sync(1, NC * 32);   // this CTA's partials are written
+            if (warp == 0 && lane == 0 && !grid_barrier(a.ticket, gridDim.x)) {
+                atomicOr(a.error, kErrTimeout);
+                flags->abort = 1;
+            }
+            named_barrier_sync(1, NC * 32);
+            // After an abort a TMA load may still be landing in the ring: no merge.
+            if (!flags->abort) merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0);
+            return;
         }
     }
     // Let the dependent merge kernel launch; it still waits for this grid to finish.

@@ -70,16 +70,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- TMA
-// 3-D tiled load into CTA shared memory, completion counted on `bar`.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
-        : "memory");
-}
-
 // 5-D tiled load into CTA shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
                                             int c3, int c4, uint32_t bar) {
@@ -92,6 +82,37 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map
 
 __device__ __forceinline__ void tma_prefetch_descriptor(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ int4 shfl_int4(int4 v, int src) {
+    return make_int4(__shfl_sync(kFullMask, v.x, src), __shfl_sync(kFullMask, v.y, src),
+                     __shfl_sync(kFullMask, v.z, src), __shfl_sync(kFullMask, v.w, src));
+}
+
+// ---------------------------------------------------------------- grid barrier
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier of a cooperative launch on a 64-bit ticket counter that
+// only ever grows: each of the `ctas` CTAs adds one per launch, so this
+// launch's barrier is complete once the counter reaches the next multiple of
+// `ctas` above this CTA's ticket (no reset between launches).  Called by one
+// thread per CTA after the CTA's own barrier; its writes before the call are
+// visible to every CTA after it.  False after the timeout.
+__device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigned ctas) {
+    __threadfence();
+    const unsigned long long mine = atomicAdd(ticket, 1ull);
+    const unsigned long long target = (mine / ctas + 1) * ctas;
+    if (ld_acquire_u64(ticket) < target) {
+        const unsigned long long start = global_ns();
+        while (ld_acquire_u64(ticket) < target)
+            if (global_ns() - start > kWaitTimeoutNs) return false;
+    }
+    __threadfence();
+    return true;
 }
 
 // ---------------------------------------------------------------- named barrier

@@ -197,6 +197,25 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     }
     if (slots > INT32_MAX / 64) return fail(PD_ERR_VALUE, "too many partial slots");
     p.num_pieces = int32_t(slots);
+    // Output rows of the split groups, merged after the decode.  With no more
+    // CTAs than SMs the decode CTAs can all be resident at once (one CTA per
+    // SM by construction), so a cooperative launch can merge them in-kernel.
+    // Each row: {output row b * Hq + query head, first slot, segments, column
+    // hh * GT + q of the [slot][HG][GT] partial layout}.
+    p.merge_rows.clear();
+    if (int64_t(L.batch) * L.query_heads > INT32_MAX) return fail(PD_ERR_VALUE, "too many output rows");
+    for (int64_t gi = 0; gi < ngroups; ++gi) {
+        const int32_t *g = &p.groups[size_t(gi) * 8];
+        if (g[5] < 0) continue;
+        for (int hh = 0; hh < hg; ++hh)
+            for (int q = 0; q < g[3]; ++q) {
+                const int64_t row = int64_t(g[0]) * L.query_heads + int64_t(g[1] + hh) * p.group + g[2] + q;
+                p.merge_rows.insert(p.merge_rows.end(),
+                                    {int32_t(row), g[5], g[6], hh * p.group_tile + q});
+            }
+    }
+    p.sm_count = sm_count;
+    p.merge_in_kernel = !p.merge_rows.empty() && sm_count > 0 && C <= sm_count;
     p.cta_off.assign(size_t(C) + 1, 0);
     p.segs.clear();
     for (int64_t i = 0; i < C; ++i) {
@@ -214,21 +233,42 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         p.cta_off[i + 1] = int32_t(p.segs.size() / 4);
     }
 
+    // Per-CTA header (64 words): [0] first segment index, [1] end index,
+    // [4..7] the first segment, [8..15] its group's 8 words, [16..47] the page
+    // ids of its first 32 pages (0 past its end).  The kernel starts streaming
+    // after reading these 256 bytes, with no further dependent loads.
+    p.head.assign(size_t(C) * 64, 0);
+    for (int64_t i = 0; i < C; ++i) {
+        int32_t *h = &p.head[size_t(i) * 64];
+        h[0] = p.cta_off[i];
+        h[1] = p.cta_off[i + 1];
+        if (h[0] == h[1]) continue;
+        const int32_t *sv = &p.segs[size_t(h[0]) * 4];
+        std::copy(sv, sv + 4, h + 4);
+        const int32_t *g = &p.groups[size_t(sv[0]) * 8];
+        std::copy(g, g + 8, h + 8);
+        for (int k = 0; k < 32 && sv[1] + k < sv[2]; ++k)
+            h[16 + k] = p.table[size_t(g[0]) * p.width + sv[1] + k];
+    }
+
     // ---------------------------------------------------------------- device image
     DeviceImage &im = p.image;
     size_t off = 0;
     im.off_error = off;    off = align256(off + 16);
-    im.off_cta = off;      off = align256(off + p.cta_off.size() * 4);
+    im.off_head = off;     off = align256(off + p.head.size() * 4);
     im.off_segs = off;     off = align256(off + p.segs.size() * 4);
     im.off_groups = off;   off = align256(off + p.groups.size() * 4);
+    im.off_merge = off;    off = align256(off + p.merge_rows.size() * 4);
     im.off_table = off;    off = align256(off + p.table.size() * 4);
     im.off_part_o = off;   off = align256(off + size_t(slots) * hg * p.group_tile * L.head_dim * 4);
     im.off_part_ml = off;  off = align256(off + size_t(slots) * hg * p.group_tile * 8);
     im.bytes = off;
     p.host_image.assign(im.off_part_o, 0);
-    std::memcpy(p.host_image.data() + im.off_cta, p.cta_off.data(), p.cta_off.size() * 4);
+    std::memcpy(p.host_image.data() + im.off_head, p.head.data(), p.head.size() * 4);
     std::memcpy(p.host_image.data() + im.off_segs, p.segs.data(), p.segs.size() * 4);
     std::memcpy(p.host_image.data() + im.off_groups, p.groups.data(), p.groups.size() * 4);
+    if (!p.merge_rows.empty())
+        std::memcpy(p.host_image.data() + im.off_merge, p.merge_rows.data(), p.merge_rows.size() * 4);
     if (!p.table.empty())
         std::memcpy(p.host_image.data() + im.off_table, p.table.data(), p.table.size() * 4);
     return PD_OK;

@@ -18,7 +18,8 @@ pd_status fail(pd_status status, const std::string &msg);
 const std::string &last_error();
 
 struct DeviceImage {
-    size_t off_error = 0, off_cta = 0, off_segs = 0, off_groups = 0;
+    // off_error: 16 bytes, the error word at +0 and the grid-barrier ticket (u64) at +8
+    size_t off_error = 0, off_head = 0, off_segs = 0, off_groups = 0, off_merge = 0;
     size_t off_table = 0, off_part_o = 0, off_part_ml = 0, bytes = 0;
 };
 
@@ -49,11 +50,15 @@ struct pd_plan {
     int32_t num_pieces = 0;        // partial slots (segments that write partials x slot_stride)
     int32_t slot_stride = 1;       // partial slots per segment: NC0 / HG sub-pipelines
     int64_t total_pages = 0;
+    int32_t sm_count = 0;          // SMs of the plan's device
+    bool merge_in_kernel = false;  // split groups merged by the decode CTAs after a grid barrier
     std::vector<int32_t> table;    // [B * W]
     std::vector<int32_t> lengths;  // [B]
     std::vector<int32_t> cta_off;  // [C + 1]
     std::vector<int32_t> segs;     // 4 per segment
     std::vector<int32_t> groups;   // 8 per group: b, kv0, qoff, nh, length, slot0 (-1: direct), segments, 0
+    std::vector<int32_t> head;        // [C][64] per-CTA header (kernel args: `head`)
+    std::vector<int32_t> merge_rows;  // 4 per merged row: out row, first slot, segments, column
     pd::DeviceImage image;
     std::vector<uint8_t> host_image;  // metadata part of the device buffer
     uint8_t *dev = nullptr;           // bound device buffer (caller-owned)

@@ -32,6 +32,7 @@ class PlanInfo(ctypes.Structure):
                 ("slot_stride", ctypes.c_int32),
                 ("group_tile", ctypes.c_int32), ("heads_per_tile", ctypes.c_int32),
                 ("total_pages", ctypes.c_int32),
+                ("merge_rows", ctypes.c_int32), ("merge_in_kernel", ctypes.c_int32),
                 ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64)]
 
 
@@ -71,7 +72,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 1:
+        if lib.pd_abi_version() != 2:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

@@ -181,10 +181,11 @@ class DecodePlan:
 
     def kernels_per_run(self, dtype=None):
         """CUDA kernels one ``run`` launches: the decode kernel, plus the dependent
-        merge kernel when some (sequence, KV-head group) was split or sub-pipelined."""
+        merge kernel when some (sequence, KV-head group) was split or sub-pipelined
+        and the decode CTAs do not merge the partials themselves."""
         import torch
         info = self.native_info(dtype if dtype is not None else torch.float16)
-        return 1 + int(info.num_pieces > 0)
+        return 1 + int(info.num_pieces > 0 and not info.merge_in_kernel)
 
     def _check_inputs(self, q, k, v):
         import torch

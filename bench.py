@@ -50,10 +50,12 @@ METRIC = "decode-attn µs/step + achieved HBM TB/s vs ~8 TB/s peak at 1/2/4/8 B2
 L2_BYTES = 126 * 2**20
 DEFAULT_STEPS, DEFAULT_WARMUP = 200, 5
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch, from
-# the ncu captures summarised in profiles/paged_decode_kernel_config2.md
-# (launch 0 of each capture; None for workloads not captured).
-NCU_TRAFFIC_BYTES = {"c2": 468_802_560 + 4_160_512, "c5": 1_073_926_912 + 5_157_376}
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch (the
+# 4th of `bench.py --workload W --steps 1 --warmup 3`), one ncu capture per
+# workload; config 4 (4.8 GB resident) was not captured.
+NCU_TRAFFIC_BYTES = {"c1": 67_258_880 + 571_648, "c2": 469_675_264 + 5_084_160,
+                     "c3a": 2_150_068_480 + 7_169_792, "c3b": 67_789_056 + 1_476_096,
+                     "c3c": 540_691_712 + 4_820_736, "c5": 1_073_953_792 + 3_577_344}
 
 
 def parse_args():

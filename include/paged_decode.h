@@ -195,6 +195,15 @@ const char *pd_status_string(pd_status status);
 const char *pd_last_error(void);     /* message of this thread's last failing call */
 int32_t pd_abi_version(void);
 
+/* Diagnostics, no reference counterpart: runs the decode kernel's two kinds
+ * of bounded wait against events that never happen -- an mbarrier phase that
+ * no thread completes (words[0]) and a grid barrier for two CTAs that only one
+ * reaches (words[1]) -- each giving up after timeout_us (1 .. 1e6) and
+ * recording PD_DEVERR_TIMEOUT in its word.  Proves the timeout path on a GPU
+ * without a fault or a hang; synchronous on the default stream of `device`.
+ */
+pd_status pd_selftest_wait_timeouts(int32_t device, uint32_t timeout_us, uint32_t *words);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,14 +58,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete; false after the timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long start = global_ns();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - start > kWaitTimeoutNs) return false;
+        if (global_ns() - start > timeout_ns) return false;
     }
 }
 
@@ -102,14 +103,15 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 // `ctas` above this CTA's ticket (no reset between launches).  Called by one
 // thread per CTA after the CTA's own barrier; its writes before the call are
 // visible to every CTA after it.  False after the timeout.
-__device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigned ctas) {
+__device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigned ctas,
+                                             unsigned long long timeout_ns = kWaitTimeoutNs) {
     __threadfence();
     const unsigned long long mine = atomicAdd(ticket, 1ull);
     const unsigned long long target = (mine / ctas + 1) * ctas;
     if (ld_acquire_u64(ticket) < target) {
         const unsigned long long start = global_ns();
         while (ld_acquire_u64(ticket) < target)
-            if (global_ns() - start > kWaitTimeoutNs) return false;
+            if (global_ns() - start > timeout_ns) return false;
     }
     __threadfence();
     return true;

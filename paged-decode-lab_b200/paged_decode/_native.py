@@ -54,6 +54,7 @@ SIGNATURES = {
     "pd_status_string": (ctypes.c_char_p, [_c_int32]),
     "pd_last_error": (ctypes.c_char_p, []),
     "pd_abi_version": (_c_int32, []),
+    "pd_selftest_wait_timeouts": (_c_int32, [_c_int32, ctypes.c_uint32, _vp]),
 }
 
 _lib = None

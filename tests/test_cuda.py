@@ -210,6 +210,87 @@ def test_result_independent_of_cta_balance_and_repeatable(dtype):
         assert plan.read_errors() == 0
 
 
+def _sm_count():
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+@pytest.mark.parametrize("dtype,dim,heads,kv_heads,page", [
+    (torch.float16, 128, 32, 8, 16), (torch.float16, 64, 16, 2, 32), (torch.float32, 64, 8, 8, 16),
+    (torch.float32, 128, 16, 4, 32), (torch.float16, 128, 32, 1, 32)])
+def test_in_kernel_merge_and_merge_kernel_agree(dtype, dim, heads, kv_heads, page):
+    """num_ctas <= SMs merges the partials inside the decode kernel (one cooperative
+    launch); more CTAs than SMs use the dependent merge kernel.  Both match the
+    oracle, and their (m, l) statistics agree."""
+    layout, table, lengths = _fragmented(3, heads, kv_heads, dim, page, [5, 3000, 6000], seed=dim + heads)
+    q, k, v = make_tensors(layout, dtype=dtype, seed=4)
+    expected = oracle(q, k, v, table, lengths)
+    tol = dict(atol=2e-3, rtol=1e-3) if dtype == torch.float16 else dict(atol=1e-5, rtol=1e-5)
+    stats_by_path = []
+    for ctas, fused in ((None, 1), (_sm_count() + 3, 0)):
+        plan = DecodePlan(layout, table, lengths, num_ctas=ctas)
+        info = plan.native_info(dtype)
+        assert plan.num_ctas == (ctas or _sm_count())   # more page tiles than CTAs
+        assert info.merge_rows > 0 and info.merge_in_kernel == fused
+        assert plan.kernels_per_run(dtype) == 2 - fused
+        out = torch.empty((3, heads, dim), device=q.device)
+        stats = torch.empty((3, heads, 2), device=q.device)
+        plan.run_with_stats(q, k, v, out, stats)
+        np.testing.assert_allclose(out.cpu().numpy(), expected, **tol)
+        torch.testing.assert_close(out, plan.run(q, k, v), rtol=0, atol=0)
+        assert plan.read_errors() == 0
+        stats_by_path.append(stats)
+    torch.testing.assert_close(stats_by_path[0], stats_by_path[1], rtol=1e-5, atol=1e-5)
+
+
+def test_in_kernel_merge_graph_replay_and_interleaved_plans():
+    """Each plan keeps its own grid-barrier count: interleaved launches of two
+    plans and CUDA-graph replays repeat the first result bit for bit."""
+    layout, table, lengths = _fragmented(4, 32, 8, 128, 16, [100, 3000, 4096, 17], seed=2)
+    q, k, v = make_tensors(layout, seed=8)
+    a = DecodePlan(layout, table, lengths)
+    b = DecodePlan(layout, table, lengths, num_ctas=37)
+    assert a.native_info(q.dtype).merge_in_kernel == 1 and b.native_info(q.dtype).merge_in_kernel == 1
+    ra, rb = a.run(q, k, v).clone(), b.run(q, k, v).clone()
+    np.testing.assert_allclose(ra.cpu().numpy(), oracle(q, k, v, table, lengths), atol=2e-3, rtol=1e-3)
+    for _ in range(60):
+        oa = a.run(q, k, v)
+        ob = b.run(q, k, v)
+    assert torch.equal(oa, ra) and torch.equal(ob, rb)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        a.run(q, k, v)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            og = a.run(q, k, v)
+        for _ in range(20):
+            graph.replay()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    assert torch.equal(og, ra)
+    assert a.read_errors() == 0 and b.read_errors() == 0
+
+
+def test_bounded_waits_time_out_with_an_error_not_a_hang():
+    """An mbarrier phase nobody completes and a grid barrier only one of two CTAs
+    reaches: both waits give up after 20 ms, record PD_DEVERR_TIMEOUT, and the
+    context stays usable."""
+    import ctypes
+    import time
+    lib = _native.load()
+    words = (ctypes.c_uint32 * 2)()
+    start = time.time()
+    assert lib.pd_selftest_wait_timeouts(torch.cuda.current_device(), 20000, words) == 0
+    assert list(words) == [1, 1]
+    assert time.time() - start < 10
+    layout, table, lengths = _fragmented(2, 8, 2, 128, 16, [40, 300], seed=1)
+    q, k, v = make_tensors(layout, seed=1)
+    plan = DecodePlan(layout, table, lengths)
+    np.testing.assert_allclose(plan.run(q, k, v).cpu().numpy(), oracle(q, k, v, table, lengths),
+                               atol=2e-3, rtol=1e-3)
+    assert plan.read_errors() == 0
+
+
 @pytest.mark.parametrize("heads,kv_heads", [(12, 1), (16, 2), (24, 1), (32, 1), (40, 2), (64, 1)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_wide_query_groups(heads, kv_heads, dtype):

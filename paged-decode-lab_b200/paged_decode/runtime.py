@@ -161,6 +161,14 @@ class DecodePlan:
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
                                 dtype=torch.float32, device=self.device)
 
+    @classmethod
+    def from_csr(cls, layout: Layout, indptr, indices, last_page_len, **kwargs):
+        """A plan from CSR paged metadata (FlashInfer's indptr / indices /
+        last_page_len form, see ``competitors.csr_to_table``)."""
+        from .competitors import csr_to_table
+        table, lengths = csr_to_table(layout, indptr, indices, last_page_len)
+        return cls(layout, table, lengths, **kwargs)
+
     @property
     def info(self):
         """pd_plan_info of the FP16 plan (see ``native_info`` for FP32)."""

@@ -271,6 +271,18 @@ def test_in_kernel_merge_graph_replay_and_interleaved_plans():
     assert a.read_errors() == 0 and b.read_errors() == 0
 
 
+def test_plan_from_csr_metadata_matches_the_table_plan():
+    """FlashInfer-style CSR metadata (indptr / indices / last_page_len) builds the
+    same plan as the page table it came from: identical output bits."""
+    from paged_decode.competitors import paged_csr
+    layout, table, lengths = _fragmented(4, 32, 8, 128, 16, [1, 700, 4096, 33], seed=6)
+    q, k, v = make_tensors(layout, seed=6)
+    indptr, indices, last = paged_csr(layout, table, lengths)
+    from_csr = DecodePlan.from_csr(layout, indptr, indices, last).run(q, k, v).clone()
+    torch.testing.assert_close(from_csr, DecodePlan(layout, table, lengths).run(q, k, v), rtol=0, atol=0)
+    np.testing.assert_allclose(from_csr.cpu().numpy(), oracle(q, k, v, table, lengths), atol=2e-3, rtol=1e-3)
+
+
 def test_bounded_waits_time_out_with_an_error_not_a_hang():
     """An mbarrier phase nobody completes and a grid barrier only one of two CTAs
     reaches: both waits give up after 20 ms, record PD_DEVERR_TIMEOUT, and the

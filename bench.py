@@ -71,6 +71,8 @@ def parse_args():
                     help="strong scaling split (default: sequence for c5, kv_head otherwise)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-competitors", action="store_true",
+                    help="skip the FlashInfer decode timed on the same inputs (1 GPU only)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     return ap.parse_args()
 
@@ -489,7 +491,56 @@ def run_ours(args, rank, local, world):
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, q, k, v, job.bytes_total, args.cpu_seconds)
+    if world == 1 and not args.no_competitors and w.dtype == "float16":
+        line["competitors"] = competitors(w, q, k, v, job, flush, args.steps)
     return line
+
+
+def competitors(w, q, k, v, job, flush, steps):
+    """FlashInfer's batch decode (the reference's measured competitor) on the same
+    caches, timed like our step; empty rows get one token (FlashInfer needs
+    nonempty contexts), so its workload is that much larger, never smaller."""
+    import torch
+    from paged_decode.competitors import FlashInferPlan
+    table, lengths = w.table.copy(), w.lengths.copy()
+    table[lengths == 0, 0] = 0
+    lengths[lengths == 0] = 1
+    out = {}
+    ours = job.decode_plan.run(q, k, v).clone()
+    for tc in (False, True):
+        key = "flashinfer" + ("_tensor_cores" if tc else "")
+        try:
+            fi = FlashInferPlan(w.layout, table, lengths, device=q.device, tensor_cores=tc)
+            for _ in range(3):
+                fi.run(q, k, v)
+            torch.cuda.synchronize()
+            if flush is None:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(steps):
+                    fi.run(q, k, v)
+                b.record()
+                torch.cuda.synchronize()
+                ms = a.elapsed_time(b) / steps
+            else:
+                times = []
+                for _ in range(steps):
+                    flush.amax()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fi.run(q, k, v)
+                    b.record()
+                    torch.cuda.synchronize()
+                    times.append(a.elapsed_time(b))
+                ms = sum(times) / steps
+            out[key] = {"version": fi.version, "us_per_step": ms * 1e3,
+                        "value": job.bytes_total / (ms * 1e-3) / 1e12, "unit": "TB/s",
+                        "max_abs_vs_ours": float((fi.out.float() - ours).abs().max()),
+                        "timing": "same as value (back to back, or L2 flushed per step)"}
+            del fi
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal
+            out[key] = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    return out
 
 
 # ---------------------------------------------------------------------- reference arm

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 2
+#define PD_ABI_VERSION 3
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -51,6 +51,7 @@ typedef enum pd_dtype { PD_FLOAT16 = 0, PD_FLOAT32 = 1 } pd_dtype;
 /* Error-word bits a kernel can raise (read with pd_plan_read_errors). */
 #define PD_DEVERR_TIMEOUT 1u      /* a bounded wait on a shared-memory barrier ran out */
 #define PD_DEVERR_BAD_PAGE 2u     /* a live page id outside [0, physical_pages): tokens skipped */
+#define PD_DEVERR_LENGTH 8u       /* a dynamic launch's length exceeded the plan's max_lengths: clamped */
 
 /* Replaces oracle.Layout (src/paged_decode/oracle.py:11-27). */
 typedef struct pd_layout {
@@ -78,6 +79,8 @@ typedef struct pd_plan_info {
     int32_t merge_rows;      /* output rows merged from partials after the decode */
     int32_t merge_in_kernel; /* 1: the decode CTAs merge them after a grid barrier (cooperative
                                 launch; num_ctas <= SMs), 0: a dependent merge kernel does */
+    int32_t dynamic;         /* 1: built by pd_plan_create_dynamic */
+    int32_t max_span;        /* longest sequence the work list covers (max_lengths, else lengths) */
     int64_t workspace_bytes; /* split-K partials + merge counters */
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
 } pd_plan_info;
@@ -97,6 +100,19 @@ typedef struct pd_plan_info {
 pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
                          const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
                          pd_dtype dtype, int32_t device, int32_t num_ctas, pd_plan **out_plan);
+
+/* A dynamic plan: as pd_plan_create, but the work list covers sequence b up
+ * to max_lengths[b] tokens (lengths[b] <= max_lengths[b] <= table_width *
+ * page_size), so that a decode loop can grow its sequences without a new
+ * plan: pd_decode_dynamic takes the live page table and lengths from device
+ * memory at every launch.  Page ids past lengths[b] may be -1 here.  No
+ * reference counterpart: the reference needs a new plan whenever a length
+ * changes (runtime.py:25-30).
+ */
+pd_status pd_plan_create_dynamic(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                                 const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
+                                 int32_t merge_mode, pd_dtype dtype, int32_t device, int32_t num_ctas,
+                                 pd_plan **out_plan);
 
 void pd_plan_destroy(pd_plan *plan);
 
@@ -142,6 +158,18 @@ pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, 
  */
 pd_status pd_decode_with_stats(pd_plan *plan, const void *q, const void *k, const void *v,
                                pd_dtype dtype, float *out, float *stats, void *stream);
+
+/* One decode step of a dynamic plan with live metadata in device memory:
+ * table int32 [batch, table_width] (the plan's width) and lengths int32
+ * [batch], read when the kernel runs, so a CUDA graph of "update metadata,
+ * decode" replays without host work.  Pages at or past lengths[b] are
+ * skipped; a length above max_lengths[b] is clamped to it and flags
+ * PD_DEVERR_LENGTH; a live page id outside [0, physical_pages) is skipped and
+ * flags PD_DEVERR_BAD_PAGE.  stats may be NULL.
+ */
+pd_status pd_decode_dynamic(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
+                            const int32_t *table, const int32_t *lengths, float *out, float *stats,
+                            void *stream);
 
 /* Max-corrected merge of per-shard results (the merge algebra of
  * oracle.py:88-96 applied across shards), as written by pd_decode_with_stats.

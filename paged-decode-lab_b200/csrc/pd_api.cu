@@ -132,7 +132,7 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.Hq = p->layout.query_heads;
     a.Hkv = p->layout.kv_heads;
     a.W = int32_t(p->width);
-    a.max_len = p->max_context;
+    a.max_len = p->max_span;
     a.group = p->group;
     a.slot_stride = p->slot_stride;
     a.num_groups = int32_t(p->groups.size() / 8);
@@ -140,6 +140,8 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.merge_rows = reinterpret_cast<const int4 *>(dev + im.off_merge);
     a.num_merge_rows = int32_t(p->merge_rows.size() / 4);
     a.fused_merge = p->merge_in_kernel ? 1 : 0;
+    a.lengths = reinterpret_cast<const int32_t *>(dev + im.off_lengths);
+    a.dynamic = p->dynamic ? 1 : 0;
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
@@ -210,7 +212,8 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
 }
 
 pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
-                      float *out, float *stats, void *stream) {
+                      float *out, float *stats, void *stream, const int32_t *table = nullptr,
+                      const int32_t *lengths = nullptr) {
     pd_status s = check_bound(p);
     if (s != PD_OK) return s;
     if ((s = check_dtype(p, dtype)) != PD_OK) return s;
@@ -222,7 +225,9 @@ pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, p
     DeviceGuard guard(p->device);
     if (guard.err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
-    const DecodeArgs args = make_args(p, q, out, stats);
+    DecodeArgs args = make_args(p, q, out, stats);
+    if (table) args.table = table;
+    if (lengths) args.lengths = lengths;
     return launch(p, k, v, dtype, kModeDecode, args, stream);
 }
 
@@ -231,9 +236,11 @@ pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, p
 
 using namespace pd;
 
-PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
-                                const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                                pd_dtype dtype, int32_t device, int32_t num_ctas, pd_plan **out_plan) {
+namespace {
+pd_status create_impl(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                      const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
+                      int32_t merge_mode, pd_dtype dtype, int32_t device, int32_t num_ctas,
+                      pd_plan **out_plan) {
     if (!out_plan) return fail(PD_ERR_VALUE, "out_plan must not be NULL");
     *out_plan = nullptr;
     int sm_count = 148;
@@ -244,8 +251,8 @@ PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, i
     }
     pd_plan *p = new (std::nothrow) pd_plan();
     if (!p) return fail(PD_ERR_VALUE, "out of host memory");
-    const pd_status s =
-        build_plan(layout, table, table_width, lengths, split_tokens, merge_mode, dtype, num_ctas, sm_count, *p);
+    const pd_status s = build_plan(layout, table, table_width, lengths, max_lengths, split_tokens, merge_mode,
+                                   dtype, num_ctas, sm_count, *p);
     if (s != PD_OK) {
         delete p;
         return s;
@@ -253,6 +260,23 @@ PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, i
     p->device = device;
     *out_plan = p;
     return PD_OK;
+}
+}  // namespace
+
+PD_API pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                                const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
+                                pd_dtype dtype, int32_t device, int32_t num_ctas, pd_plan **out_plan) {
+    return create_impl(layout, table, table_width, lengths, nullptr, split_tokens, merge_mode, dtype, device,
+                       num_ctas, out_plan);
+}
+
+PD_API pd_status pd_plan_create_dynamic(const pd_layout *layout, const int32_t *table, int64_t table_width,
+                                        const int32_t *lengths, const int32_t *max_lengths,
+                                        int32_t split_tokens, int32_t merge_mode, pd_dtype dtype,
+                                        int32_t device, int32_t num_ctas, pd_plan **out_plan) {
+    if (!max_lengths) return fail(PD_ERR_VALUE, "max_lengths must not be NULL");
+    return create_impl(layout, table, table_width, lengths, max_lengths, split_tokens, merge_mode, dtype,
+                       device, num_ctas, out_plan);
 }
 
 PD_API void pd_plan_destroy(pd_plan *plan) { delete plan; }
@@ -271,6 +295,8 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->total_pages = int32_t(p->total_pages);
     info->merge_rows = int32_t(p->merge_rows.size() / 4);
     info->merge_in_kernel = p->merge_in_kernel ? 1 : 0;
+    info->dynamic = p->dynamic ? 1 : 0;
+    info->max_span = p->max_span;
     info->workspace_bytes = int64_t(p->image.bytes - p->image.off_part_o);
     info->device_bytes = int64_t(p->image.bytes);
     return PD_OK;
@@ -311,6 +337,16 @@ PD_API pd_status pd_plan_bind(pd_plan *p, void *buffer, size_t bytes, void *stre
 PD_API pd_status pd_decode(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
                            float *out, void *stream) {
     return decode_impl(p, q, k, v, dtype, out, nullptr, stream);
+}
+
+PD_API pd_status pd_decode_dynamic(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
+                                   const int32_t *table, const int32_t *lengths, float *out, float *stats,
+                                   void *stream) {
+    if (p && !p->dynamic) return fail(PD_ERR_VALUE, "plan was not built by pd_plan_create_dynamic");
+    if (!table || !lengths) return fail(PD_ERR_VALUE, "table and lengths must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(lengths)) & 3)
+        return fail(PD_ERR_VALUE, "table and lengths must be 4-byte aligned");
+    return decode_impl(p, q, k, v, dtype, out, stats, stream, table, lengths);
 }
 
 PD_API pd_status pd_decode_with_stats(pd_plan *p, const void *q, const void *k, const void *v,

@@ -32,6 +32,7 @@
 // this is the reference's exp(s - m) rewritten, not a different softmax.
 #pragma once
 
+#include <climits>
 #include <type_traits>
 
 #include "pd_device.cuh"
@@ -60,12 +61,18 @@ struct DecodeArgs {
     const int4 *merge_rows;      // split groups' rows: {out row, slot0, segments, head * GT + query head}
     int32_t num_merge_rows;
     int32_t fused_merge;         // 1: the CTAs merge the partials after a grid barrier
+    // Dynamic plans: groups cover each sequence up to its capacity (group word
+    // 4); the live length of sequence b is min(lengths[b], capacity), pages at
+    // or past it are skipped, and page ids always come from `table`.
+    const int32_t *lengths;
+    int32_t dynamic;
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
 };
 
 constexpr uint32_t kErrTimeout = 1u;
 constexpr uint32_t kErrBadPage = 2u;
+constexpr uint32_t kErrLength = 8u;
 
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS>
 struct KernelShape {
@@ -644,10 +651,13 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             bool ng0_loaded = !more;
             const int32_t *trow = a.table + int64_t(g0.x) * a.W;
             const int kv0 = g0.y;
+            // dynamic plans: pages at or past the live length are skipped
+            const int live_end = a.dynamic ? max(0, a.lengths[g0.x]) : INT_MAX;
             for (int pg = sg.y; pg < sg.z; pg += 32) {
                 const int n = min(32, sg.z - pg);
-                const int mine = (si == seg_begin && pg == sg.y) ? first_pages
-                                                                 : (lane < n ? __ldg(trow + pg + lane) : 0);
+                const int mine = (!a.dynamic && si == seg_begin && pg == sg.y)
+                                     ? first_pages
+                                     : (lane < n ? __ldg(trow + pg + lane) : 0);
                 for (int i = 0; i < n; ++i, ++j) {
                     const int page = __shfl_sync(kFullMask, mine, i);
                     if (lane == 0 && !stop) {
@@ -659,6 +669,9 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                             if (!flags->abort) atomicOr(a.error, kErrTimeout);
                             flags->abort = 1;
                             stop = true;
+                        } else if (int64_t(pg + i) * T >= live_end) {
+                            slot_valid[slot] = 0;   // not live yet: nothing to stream
+                            mbar_arrive(fb);
                         } else if (page >= 0 && int64_t(page) < a.P) {
                             slot_valid[slot] = 1;
                             mbar_arrive_expect_tx(fb, S::TILE_BYTES);
@@ -700,7 +713,12 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         const int4 g0 = si == seg_begin ? g0_h : a.groups[2 * sg.x];
         const int4 g1 = si == seg_begin ? g1_h : a.groups[2 * sg.x + 1];
         const int b = g0.x, kv0 = g0.y, qoff = g0.z, nh = g0.w;
-        const int length = g1.x;
+        int length = g1.x;
+        if (a.dynamic) {
+            const int live = a.lengths[b];
+            if (live > length && warp == 0 && lane == 0) atomicOr(a.error, kErrLength);
+            length = min(max(live, 0), length);
+        }
         const int npg = sg.z - sg.y;
         const int first = ((sub - j) % NSUB + NSUB) % NSUB;
 

@@ -43,8 +43,9 @@ pd_status fail(pd_status status, const std::string &msg) {
 const std::string &last_error() { return g_last_error; }
 
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
-                     const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                     pd_dtype dtype, int32_t num_ctas, int32_t sm_count, pd_plan &p) {
+                     const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
+                     int32_t merge_mode, pd_dtype dtype, int32_t num_ctas, int32_t sm_count,
+                     pd_plan &p) {
     if (!layout) return fail(PD_ERR_VALUE, "layout must not be NULL");
     const pd_layout L = *layout;
     // Layout.__post_init__ (oracle.py:24-27)
@@ -85,9 +86,18 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         }
     }
     if (width > 65536) return fail(PD_ERR_VALUE, "page table width must not exceed 65536");
-    int32_t max_context = 0;
-    for (int b = 0; b < L.batch; ++b) max_context = std::max(max_context, lengths[b]);
-    if (max_context > 1048576)
+    // A dynamic plan's work covers each sequence up to its capacity.
+    if (max_lengths)
+        for (int b = 0; b < L.batch; ++b)
+            if (max_lengths[b] < lengths[b] || max_lengths[b] > capacity)
+                return fail(PD_ERR_VALUE, "max_lengths must lie between lengths and the page table capacity");
+    const int32_t *span = max_lengths ? max_lengths : lengths;
+    int32_t max_context = 0, max_span = 0;
+    for (int b = 0; b < L.batch; ++b) {
+        max_context = std::max(max_context, lengths[b]);
+        max_span = std::max(max_span, span[b]);
+    }
+    if (max_span > 1048576)
         return fail(PD_ERR_VALUE, "this implementation supports at most 1M context tokens");
     const int64_t splits = std::max<int64_t>(1, (int64_t(max_context) + split_tokens - 1) / split_tokens);
     if (splits > 65535) return fail(PD_ERR_VALUE, "too many context splits");
@@ -102,6 +112,8 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     p.dtype = dtype;
     p.splits = int32_t(splits);
     p.max_context = max_context;
+    p.max_span = max_span;
+    p.dynamic = max_lengths != nullptr;
     p.group = L.query_heads / L.kv_heads;
     p.group_tile = p.group <= 8 ? 8 : (p.group <= 16 ? 16 : 32);
     p.group_splits = (p.group + p.group_tile - 1) / p.group_tile;
@@ -138,10 +150,10 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
                 g[1] = kg * hg;                        // first KV head of the group
                 g[2] = gs * p.group_tile;              // query-head offset inside each KV head's group
                 g[3] = std::min(p.group_tile, p.group - gs * p.group_tile);
-                g[4] = lengths[b];
+                g[4] = span[b];                        // tokens the group's work covers
                 g[5] = -1;
                 g[6] = 0;
-                gpages[gi] = (int64_t(lengths[b]) + T - 1) / T;
+                gpages[gi] = (int64_t(span[b]) + T - 1) / T;
                 total += gpages[gi];
             }
     if (total > INT32_MAX) return fail(PD_ERR_VALUE, "too many page tiles per decode step");
@@ -259,6 +271,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     im.off_segs = off;     off = align256(off + p.segs.size() * 4);
     im.off_groups = off;   off = align256(off + p.groups.size() * 4);
     im.off_merge = off;    off = align256(off + p.merge_rows.size() * 4);
+    im.off_lengths = off;  off = align256(off + p.lengths.size() * 4);
     im.off_table = off;    off = align256(off + p.table.size() * 4);
     im.off_part_o = off;   off = align256(off + size_t(slots) * hg * p.group_tile * L.head_dim * 4);
     im.off_part_ml = off;  off = align256(off + size_t(slots) * hg * p.group_tile * 8);
@@ -269,6 +282,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     std::memcpy(p.host_image.data() + im.off_groups, p.groups.data(), p.groups.size() * 4);
     if (!p.merge_rows.empty())
         std::memcpy(p.host_image.data() + im.off_merge, p.merge_rows.data(), p.merge_rows.size() * 4);
+    std::memcpy(p.host_image.data() + im.off_lengths, p.lengths.data(), p.lengths.size() * 4);
     if (!p.table.empty())
         std::memcpy(p.host_image.data() + im.off_table, p.table.data(), p.table.size() * 4);
     return PD_OK;

@@ -19,7 +19,7 @@ const std::string &last_error();
 
 struct DeviceImage {
     // off_error: 16 bytes, the error word at +0 and the grid-barrier ticket (u64) at +8
-    size_t off_error = 0, off_head = 0, off_segs = 0, off_groups = 0, off_merge = 0;
+    size_t off_error = 0, off_head = 0, off_segs = 0, off_groups = 0, off_merge = 0, off_lengths = 0;
     size_t off_table = 0, off_part_o = 0, off_part_ml = 0, bytes = 0;
 };
 
@@ -52,6 +52,8 @@ struct pd_plan {
     int64_t total_pages = 0;
     int32_t sm_count = 0;          // SMs of the plan's device
     bool merge_in_kernel = false;  // split groups merged by the decode CTAs after a grid barrier
+    bool dynamic = false;          // work covers max_lengths; live lengths / table read at launch
+    int32_t max_span = 0;          // longest sequence the work list covers (max_lengths or lengths)
     std::vector<int32_t> table;    // [B * W]
     std::vector<int32_t> lengths;  // [B]
     std::vector<int32_t> cta_off;  // [C + 1]
@@ -70,8 +72,12 @@ namespace pd {
 
 // Validate metadata and build the balanced work list; `sm_count` is used when
 // num_ctas <= 0.  Mirrors the checks of runtime.py:33-51 and oracle.py:20-47.
+// `max_lengths` (nullable) makes a dynamic plan: its work list covers
+// sequence b up to max_lengths[b] tokens, and launches may pass live lengths
+// <= max_lengths and a page table updated on the device.
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
-                     const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
-                     pd_dtype dtype, int32_t num_ctas, int32_t sm_count, pd_plan &plan);
+                     const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
+                     int32_t merge_mode, pd_dtype dtype, int32_t num_ctas, int32_t sm_count,
+                     pd_plan &plan);
 
 }  // namespace pd

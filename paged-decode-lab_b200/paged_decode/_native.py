@@ -33,18 +33,22 @@ class PlanInfo(ctypes.Structure):
                 ("group_tile", ctypes.c_int32), ("heads_per_tile", ctypes.c_int32),
                 ("total_pages", ctypes.c_int32),
                 ("merge_rows", ctypes.c_int32), ("merge_in_kernel", ctypes.c_int32),
+                ("dynamic", ctypes.c_int32), ("max_span", ctypes.c_int32),
                 ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64)]
 
 
 SIGNATURES = {
     "pd_plan_create": (_c_int32, [ctypes.POINTER(Layout), _vp, _c_int64, _vp, _c_int32, _c_int32,
                                   _c_int32, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
+    "pd_plan_create_dynamic": (_c_int32, [ctypes.POINTER(Layout), _vp, _c_int64, _vp, _vp, _c_int32,
+                                          _c_int32, _c_int32, _c_int32, _c_int32, ctypes.POINTER(_vp)]),
     "pd_plan_destroy": (None, [_vp]),
     "pd_plan_get_info": (_c_int32, [_vp, ctypes.POINTER(PlanInfo)]),
     "pd_plan_copy_worklist": (_c_int32, [_vp, _vp, _vp, _vp]),
     "pd_plan_device_bytes": (_c_size, [_vp]),
     "pd_plan_bind": (_c_int32, [_vp, _vp, _c_size, _vp]),
     "pd_decode": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
+    "pd_decode_dynamic": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp, _vp, _vp]),
     "pd_decode_with_stats": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
@@ -73,7 +77,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 2:
+        if lib.pd_abi_version() != 3:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

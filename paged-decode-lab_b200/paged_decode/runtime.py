@@ -43,17 +43,25 @@ def _check_limits(layout, split_tokens, merge):
         raise ValueError("split_tokens must be an integer in [1,1048576]")
 
 
-def _native_plan(layout, table, lengths, split_tokens, merge, dtype_code, device_index, num_ctas):
+def _native_plan(layout, table, lengths, split_tokens, merge, dtype_code, device_index, num_ctas,
+                 max_lengths=None):
     lib = _native.load()
     c_layout = _native.Layout(layout.batch, layout.query_heads, layout.kv_heads, layout.head_dim,
                               layout.page_size, layout.physical_pages)
     table = np.ascontiguousarray(table, dtype=np.int32)
     lengths = np.ascontiguousarray(lengths, dtype=np.int32)
     handle = ctypes.c_void_p()
-    _native.check(lib.pd_plan_create(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
-                                     lengths.ctypes.data, split_tokens, int(merge == "shared"),
-                                     dtype_code, device_index, num_ctas or 0, ctypes.byref(handle)),
-                  "plan")
+    if max_lengths is None:
+        status = lib.pd_plan_create(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
+                                    lengths.ctypes.data, split_tokens, int(merge == "shared"),
+                                    dtype_code, device_index, num_ctas or 0, ctypes.byref(handle))
+    else:
+        max_lengths = np.ascontiguousarray(max_lengths, dtype=np.int32)
+        status = lib.pd_plan_create_dynamic(ctypes.byref(c_layout), table.ctypes.data, table.shape[1],
+                                            lengths.ctypes.data, max_lengths.ctypes.data, split_tokens,
+                                            int(merge == "shared"), dtype_code, device_index,
+                                            num_ctas or 0, ctypes.byref(handle))
+    _native.check(status, "plan")
     return handle
 
 
@@ -71,7 +79,8 @@ def _worklist(lib, handle):
 _DTYPE_CODES = {"float16": _native.PD_FLOAT16, "float32": _native.PD_FLOAT32}
 
 
-def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=148, dtype="float16"):
+def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=148, dtype="float16",
+                 max_lengths=None):
     """Build a host-only plan (no GPU needed) for one input dtype and return its work list.
 
     Returns a dict with ``info`` (pd_plan_info fields), ``segments``
@@ -83,7 +92,8 @@ def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=1
     _check_limits(layout, split_tokens, "serial")
     table, lengths = validate_metadata(layout, table, lengths)
     lib = _native.load()
-    handle = _native_plan(layout, table, lengths, split_tokens, "serial", _DTYPE_CODES[dtype], -1, num_ctas)
+    handle = _native_plan(layout, table, lengths, split_tokens, "serial", _DTYPE_CODES[dtype], -1, num_ctas,
+                          max_lengths)
     try:
         info, segs, groups, offsets = _worklist(lib, handle)
     finally:
@@ -95,11 +105,12 @@ def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=1
 class _NativePlan:
     """One C-ABI plan (one input dtype) and the device buffer it is bound to."""
 
-    def __init__(self, lib, layout, table, lengths, split_tokens, merge, dtype_code, device, num_ctas):
+    def __init__(self, lib, layout, table, lengths, split_tokens, merge, dtype_code, device, num_ctas,
+                 max_lengths=None):
         import torch
         self._lib = lib
         self.handle = _native_plan(layout, table, lengths, split_tokens, merge, dtype_code,
-                                   device.index, num_ctas)
+                                   device.index, num_ctas, max_lengths)
         self.info, self.segments, self.groups, self.cta_offsets = _worklist(lib, self.handle)
         nbytes = int(lib.pd_plan_device_bytes(self.handle))
         self.buffer = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
@@ -131,10 +142,18 @@ class DecodePlan:
     """
 
     def __init__(self, layout: Layout, table, lengths, *, device="cuda", split_tokens=256,
-                 merge="serial", num_ctas=None):
+                 merge="serial", num_ctas=None, max_lengths=None):
         import torch
         _check_limits(layout, split_tokens, merge)
         table, lengths = validate_metadata(layout, table, lengths)
+        if max_lengths is not None:
+            max_lengths = np.asarray(max_lengths)
+            if max_lengths.shape != lengths.shape or max_lengths.dtype.kind not in "iu":
+                raise ValueError("max_lengths must be integers of shape [batch]")
+            if (max_lengths < lengths).any() or (max_lengths > table.shape[1] * layout.page_size).any():
+                raise ValueError("max_lengths must lie between lengths and the page table capacity")
+            max_lengths = max_lengths.astype(np.int32)
+        self.max_lengths = max_lengths
         if table.shape[1] > 65536:
             raise ValueError("page table width must not exceed 65536")
         self.max_context = int(lengths.max(initial=0))
@@ -156,7 +175,7 @@ class DecodePlan:
         self._lib = _native.load()
         # one native plan per input dtype (page tiles are sized per dtype)
         self._native = {code: _NativePlan(self._lib, layout, table, lengths, split_tokens, merge, code,
-                                          self.device, num_ctas)
+                                          self.device, num_ctas, max_lengths)
                         for code in (_native.PD_FLOAT16, _native.PD_FLOAT32)}
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
                                 dtype=torch.float32, device=self.device)
@@ -241,10 +260,47 @@ class DecodePlan:
             stats.data_ptr(), stream), "decode")
         return out, stats
 
+    def run_dynamic(self, q, k, v, table, lengths, out=None, stats=None):
+        """Decode with live metadata in device memory (plans built with ``max_lengths``).
+
+        ``table`` int32 [B, W] (this plan's width) and ``lengths`` int32 [B] are
+        CUDA tensors read when the kernel runs, so a decode loop can append
+        tokens and pages on the device, inside a CUDA graph, without a new
+        plan.  Lengths above ``max_lengths`` are clamped and flag
+        PD_DEVERR_LENGTH (``read_errors``).  Returns ``out`` (default: the
+        plan's borrowed output).
+        """
+        import torch
+        if self.max_lengths is None:
+            raise ValueError("run_dynamic needs a plan built with max_lengths")
+        dtype = self._check_inputs(q, k, v)
+        layout = self.layout
+        width = self._table_cpu.shape[1]
+        for t, shape in ((table, (layout.batch, width)), (lengths, (layout.batch,))):
+            if not isinstance(t, torch.Tensor) or t.dtype != torch.int32 or tuple(t.shape) != shape or \
+                    t.device != self.device or not t.is_contiguous():
+                raise ValueError("table/lengths must be contiguous int32 CUDA tensors of shape "
+                                 "[batch, table width] / [batch] on the plan device")
+        out = self._out if out is None else out
+        rows = (layout.batch, layout.query_heads)
+        if tuple(out.shape) != rows + (layout.head_dim,) or out.dtype != torch.float32 or \
+                out.device != self.device or not out.is_contiguous():
+            raise ValueError("out must be contiguous FP32 [B,Hq,D] on the plan device")
+        if stats is not None and (tuple(stats.shape) != rows + (2,) or stats.dtype != torch.float32 or
+                                  stats.device != self.device or not stats.is_contiguous()):
+            raise ValueError("stats must be contiguous FP32 [B,Hq,2] on the plan device")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(self._lib.pd_decode_dynamic(
+            self._native[dtype].handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), dtype,
+            table.data_ptr(), lengths.data_ptr(), out.data_ptr(),
+            None if stats is None else stats.data_ptr(), stream), "decode")
+        return out
+
     def gather(self, k, v):
         """Debug: the live K/V rows of every (sequence, KV head) through the kernel's TMA path.
 
-        Returns dense [B, Hkv, max_context, D] tensors in the cache dtype; rows
+        Returns dense [B, Hkv, max_context (max(max_lengths) for a dynamic plan), D]
+        tensors in the cache dtype; rows
         past a sequence's length are zero.
         """
         import torch
@@ -252,7 +308,8 @@ class DecodePlan:
         q_stub = torch.empty((layout.batch, layout.query_heads, layout.head_dim), dtype=k.dtype,
                              device=self.device)
         dtype = self._check_inputs(q_stub, k, v)
-        shape = (layout.batch, layout.kv_heads, max(self.max_context, 1), layout.head_dim)
+        span = int(self.max_lengths.max(initial=0)) if self.max_lengths is not None else self.max_context
+        shape = (layout.batch, layout.kv_heads, max(span, 1), layout.head_dim)
         dense_k = torch.zeros(shape, dtype=k.dtype, device=self.device)
         dense_v = torch.zeros(shape, dtype=k.dtype, device=self.device)
         stream = torch.cuda.current_stream(self.device).cuda_stream

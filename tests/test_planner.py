@@ -142,3 +142,21 @@ def test_heads_per_tile_targets_64kib_fp16_32kib_fp32_tiles(dim, page, kv_heads,
     plan = inspect_plan(layout, np.arange(8, dtype=np.int32).reshape(2, 4), [page * 4, 1], num_ctas=3,
                         dtype=dtype)
     assert plan["info"]["heads_per_tile"] == expected
+
+
+def test_dynamic_plan_covers_each_sequence_up_to_its_capacity():
+    """A dynamic plan's groups and segments cover max_lengths, not lengths."""
+    layout = Layout(3, 8, 2, 128, 16, 30)
+    table = np.arange(30, dtype=np.int32).reshape(3, 10)
+    table[0, 2:] = -1                      # pages past the live length may be unallocated
+    lengths = np.array([20, 0, 100], dtype=np.int32)
+    max_lengths = np.array([60, 5, 160], dtype=np.int32)
+    plan = inspect_plan(layout, table, lengths, num_ctas=7, max_lengths=max_lengths)
+    assert plan["info"]["dynamic"] == 1 and plan["info"]["max_span"] == 160
+    check_worklist(layout, table, max_lengths, plan)
+    static = inspect_plan(layout, np.arange(30, dtype=np.int32).reshape(3, 10), lengths, num_ctas=7)
+    assert static["info"]["dynamic"] == 0 and static["info"]["max_span"] == 100
+    with pytest.raises(ValueError, match="max_lengths"):
+        inspect_plan(layout, table, lengths, num_ctas=7, max_lengths=np.array([60, 5, 161]))
+    with pytest.raises(ValueError, match="max_lengths"):
+        inspect_plan(layout, table, lengths, num_ctas=7, max_lengths=np.array([19, 5, 160]))

@@ -633,6 +633,9 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
 
     if (warp == NC) {
         // ------------------------------------------------------------ producer
+        // Tiles of 8 KiB or less (one KV head, page 16) need more than one
+        // thread issuing; larger ones keep a single issuing lane (measured).
+        constexpr int PL = (S::TILE_BYTES <= 8192 && SLOTS >= 8) ? 4 : 1;
         if (lane == 0) {
             tma_prefetch_descriptor(&tm_k);
             tma_prefetch_descriptor(&tm_v);
@@ -658,18 +661,22 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                 const int mine = (!a.dynamic && si == seg_begin && pg == sg.y)
                                      ? first_pages
                                      : (lane < n ? __ldg(trow + pg + lane) : 0);
-                for (int i = 0; i < n; ++i, ++j) {
-                    const int page = __shfl_sync(kFullMask, mine, i);
-                    if (lane == 0 && !stop) {
-                        const int slot = j % SLOTS;
-                        const int use = j / SLOTS;
+                // PL lanes issue PL consecutive tiles side by side, so one
+                // TMA instruction carries PL tiles.
+                for (int i = 0; i < n; i += PL) {
+                    const int cnt = min(PL, n - i);
+                    const int page = __shfl_sync(kFullMask, mine, (i + lane) & 31);
+                    if (lane < cnt && !stop) {
+                        const int jj = j + lane;
+                        const int slot = jj % SLOTS;
+                        const int use = jj / SLOTS;
                         const uint32_t fb = smem_u32(full_bar + slot);
                         if (flags->abort ||
                             (use > 0 && !mbar_wait(smem_u32(empty_bar + slot), (use - 1) & 1))) {
                             if (!flags->abort) atomicOr(a.error, kErrTimeout);
                             flags->abort = 1;
                             stop = true;
-                        } else if (int64_t(pg + i) * T >= live_end) {
+                        } else if (int64_t(pg + i + lane) * T >= live_end) {
                             slot_valid[slot] = 0;   // not live yet: nothing to stream
                             mbar_arrive(fb);
                         } else if (page >= 0 && int64_t(page) < a.P) {
@@ -687,6 +694,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                             mbar_arrive(fb);
                         }
                     }
+                    j += cnt;
                 }
                 if (!ng0_loaded) {
                     ng0 = __ldg(a.groups + 2 * nsg.x);

@@ -69,6 +69,8 @@ def parse_args():
                     help="N > 1: weak = KV-head shards of an N x larger model; strong = split this config")
     ap.add_argument("--sharding", choices=["kv_head", "sequence"], default=None,
                     help="strong scaling split (default: sequence for c5, kv_head otherwise)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="sequence sharding: one kernel with NVLink peer stores, or NCCL all-gather + merge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-competitors", action="store_true",
@@ -274,6 +276,7 @@ class RankJob:
         self.sharding = "none"
         self.bytes_total = algorithmic_bytes(w)
         self.extra_kernels = 0
+        self.close = lambda: None
         if world == 1:
             from paged_decode.runtime import DecodePlan
             self.plan = DecodePlan(L, w.table, w.lengths, split_tokens=w.split_tokens)
@@ -317,15 +320,22 @@ class RankJob:
             loc = Layout(L.batch, L.query_heads, L.kv_heads, L.head_dim, L.page_size, max(1, len(ids)))
             local = workload.Workload(w.name, loc, ltab, ll, w.split_tokens, dtype=w.dtype, std=w.std,
                                       seed=w.seed + rank)
-            plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, split_tokens=w.split_tokens)
+            plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, split_tokens=w.split_tokens,
+                                               exchange=args.exchange)
             self.q, self.k, self.v = local.tensors("cuda")
             self.run = lambda q: plan.run(q, self.k, self.v)
+            self.close = plan.close
             self.decode_plan = plan.plan
             self.bytes_rank = algorithmic_bytes(local)
-            self.extra_kernels = 1                      # the cross-shard merge (NCCL's own kernel not counted)
             self.nvlink_bytes = plan.nvlink_bytes_per_step
-            self.sharding = (f"sequence, strong: rank r owns logical pages [{lo}, {hi}) of every sequence; "
-                             f"all_gather of {pd_dist.packed_size(loc) * 4} B per rank + max-corrected merge")
+            if args.exchange == "peer":
+                self.extra_kernels = -self.decode_plan.kernels_per_run(self.q.dtype) + 1   # one kernel a step
+                how = (f"one kernel per rank: decode, NVLink peer stores of {pd_dist.packed_size(loc) * 4} B "
+                       "into every rank's buffer, bounded wait for all ranks, max-corrected merge")
+            else:
+                self.extra_kernels = 1                  # the cross-shard merge (NCCL's own kernel not counted)
+                how = f"NCCL all_gather of {pd_dist.packed_size(loc) * 4} B per rank + max-corrected merge"
+            self.sharding = f"sequence, strong: rank r owns logical pages [{lo}, {hi}) of every sequence; {how}"
 
     def kernels_per_step(self):
         return self.decode_plan.kernels_per_run(self.q.dtype) + self.extra_kernels
@@ -493,6 +503,7 @@ def run_ours(args, rank, local, world):
         line["cpu_baseline"] = cpu_baseline(w, q, k, v, job.bytes_total, args.cpu_seconds)
     if world == 1 and not args.no_competitors and w.dtype == "float16":
         line["competitors"] = competitors(w, q, k, v, job, flush, args.steps)
+    job.close()
     return line
 
 

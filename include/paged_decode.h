@@ -223,6 +223,32 @@ const char *pd_status_string(pd_status status);
 const char *pd_last_error(void);     /* message of this thread's last failing call */
 int32_t pd_abi_version(void);
 
+/* ------------------------------------------------------------------------
+ * Sequence sharding over NVLink peer memory, one kernel per rank per step.
+ * No reference counterpart (the reference never ran on more than one GPU).
+ *
+ * Each rank holds one exchange buffer of pd_exchange_bytes() bytes, made by
+ * pd_exchange_alloc (cudaMalloc + a CUDA IPC handle) and opened by every
+ * other rank of the node with pd_exchange_open.  pd_decode_exchange decodes
+ * this rank's pages (its plan covers its share of every sequence) and stores
+ * each finished row (normalised o, m, l) into this rank's slot of every
+ * rank's buffer, then signals every rank with a system-scope atomic, waits
+ * (bounded, PD_DEVERR_TIMEOUT) until all `total_ctas` CTAs of all ranks have
+ * signalled, and merges the ranks' rows into out (and stats when not NULL)
+ * with the max-corrected merge.  Every rank must call it once per step, in
+ * the same order, with buffers[s] = rank s's buffer as seen from this GPU
+ * (buffers[rank] = its own); total_ctas = the sum of every rank's num_ctas
+ * (<= 1024 each).  No multicast and no library kernel touches peer memory.
+ */
+size_t pd_exchange_bytes(const pd_plan *plan, int32_t world);
+pd_status pd_exchange_alloc(int32_t device, size_t bytes, void **buffer, void *ipc_handle /* 64 bytes */);
+pd_status pd_exchange_open(int32_t device, const void *ipc_handle, void **peer_buffer);
+pd_status pd_exchange_close(int32_t device, void *peer_buffer);
+pd_status pd_exchange_free(int32_t device, void *buffer);
+pd_status pd_decode_exchange(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
+                             void *const *buffers, int32_t rank, int32_t world, int32_t total_ctas,
+                             float *out, float *stats, void *stream);
+
 /* Diagnostics, no reference counterpart: runs the decode kernel's two kinds
  * of bounded wait against events that never happen -- an mbarrier phase that
  * no thread completes (words[0]) and a grid barrier for two CTAs that only one

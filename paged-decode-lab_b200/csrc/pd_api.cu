@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <mutex>
 #include <new>
 #include <set>
@@ -142,6 +143,8 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.fused_merge = p->merge_in_kernel ? 1 : 0;
     a.lengths = reinterpret_cast<const int32_t *>(dev + im.off_lengths);
     a.dynamic = p->dynamic ? 1 : 0;
+    a.xworld = 0;
+    a.rows = p->layout.batch * p->layout.query_heads;
     a.P = p->layout.physical_pages;
     a.scale_log2 = float(1.4426950408889634 / std::sqrt(double(p->layout.head_dim)));
     return a;
@@ -188,13 +191,14 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     attr[1].val.cooperative = 1;
     cfg.attrs = attr;
     cudaError_t err;
-    if (la.fused_merge) {
-        // The CTAs wait for each other at a grid barrier before merging; a
-        // cooperative launch guarantees they are all resident, or refuses.
+    if (la.fused_merge || la.xworld) {
+        // The CTAs wait for each other at a grid barrier before merging, and
+        // in exchange mode for every CTA of every rank; a cooperative launch
+        // guarantees they are all resident, or refuses.
         cfg.numAttrs = 2;
         err = cudaLaunchKernelEx(&cfg, e.fn, tc.map_k, tc.map_v, la);
         if (err == cudaSuccess) return PD_OK;
-        if (err != cudaErrorCooperativeLaunchTooLarge)
+        if (err != cudaErrorCooperativeLaunchTooLarge || la.xworld)
             return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
         (void)cudaGetLastError();   // not all CTAs fit at once: merge with the separate kernel
         la.fused_merge = 0;
@@ -213,7 +217,7 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
 
 pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
                       float *out, float *stats, void *stream, const int32_t *table = nullptr,
-                      const int32_t *lengths = nullptr) {
+                      const int32_t *lengths = nullptr, const DecodeArgs *exchange = nullptr) {
     pd_status s = check_bound(p);
     if (s != PD_OK) return s;
     if ((s = check_dtype(p, dtype)) != PD_OK) return s;
@@ -228,7 +232,19 @@ pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, p
     DecodeArgs args = make_args(p, q, out, stats);
     if (table) args.table = table;
     if (lengths) args.lengths = lengths;
+    if (exchange) {
+        std::copy(exchange->xpeer, exchange->xpeer + kMaxRanks, args.xpeer);
+        args.xslot = exchange->xslot;
+        args.xrank = exchange->xrank;
+        args.xworld = exchange->xworld;
+        args.xtotal_ctas = exchange->xtotal_ctas;
+    }
     return launch(p, k, v, dtype, kModeDecode, args, stream);
+}
+
+int64_t exchange_slot_bytes(const pd_plan *p) {
+    const int64_t rows = int64_t(p->layout.batch) * p->layout.query_heads;
+    return (rows * (p->layout.head_dim + 2) * 4 + 255) / 256 * 256;
 }
 
 }  // namespace
@@ -491,3 +507,78 @@ PD_API const char *pd_status_string(pd_status status) {
 PD_API const char *pd_last_error(void) { return pd::last_error().c_str(); }
 
 PD_API int32_t pd_abi_version(void) { return PD_ABI_VERSION; }
+
+// ------------------------------------------------------------------ peer exchange (sequence sharding)
+PD_API size_t pd_exchange_bytes(const pd_plan *p, int32_t world) {
+    if (!p || world < 1 || world > kMaxRanks) return 0;
+    return size_t(kXRecv + 2 * int64_t(world) * exchange_slot_bytes(p));
+}
+
+PD_API pd_status pd_exchange_alloc(int32_t device, size_t bytes, void **buffer, void *ipc_handle) {
+    if (!buffer || !ipc_handle || bytes == 0) return fail(PD_ERR_VALUE, "buffer, ipc_handle and bytes are required");
+    *buffer = nullptr;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    void *ptr = nullptr;
+    cudaError_t err = cudaMalloc(&ptr, bytes);
+    if (err == cudaSuccess) err = cudaMemset(ptr, 0, bytes);   // arrival counter and launch counts start at 0
+    cudaIpcMemHandle_t h;
+    if (err == cudaSuccess) err = cudaIpcGetMemHandle(&h, ptr);
+    if (err != cudaSuccess) {
+        if (ptr) cudaFree(ptr);
+        return fail(PD_ERR_CUDA, std::string("exchange buffer: ") + cudaGetErrorString(err));
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *buffer = ptr;
+    return PD_OK;
+}
+
+PD_API pd_status pd_exchange_open(int32_t device, const void *ipc_handle, void **peer_buffer) {
+    if (!ipc_handle || !peer_buffer) return fail(PD_ERR_VALUE, "ipc_handle and peer_buffer are required");
+    *peer_buffer = nullptr;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    const cudaError_t err = cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return fail(PD_ERR_CUDA, std::string("peer buffer: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
+PD_API pd_status pd_exchange_close(int32_t device, void *peer_buffer) {
+    DeviceGuard guard(device);
+    const cudaError_t err = cudaIpcCloseMemHandle(peer_buffer);
+    if (err != cudaSuccess) return fail(PD_ERR_CUDA, std::string("close peer buffer: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
+PD_API pd_status pd_exchange_free(int32_t device, void *buffer) {
+    DeviceGuard guard(device);
+    const cudaError_t err = cudaFree(buffer);
+    if (err != cudaSuccess) return fail(PD_ERR_CUDA, std::string("free exchange buffer: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
+PD_API pd_status pd_decode_exchange(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
+                                    void *const *buffers, int32_t rank, int32_t world, int32_t total_ctas,
+                                    float *out, float *stats, void *stream) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+        return fail(PD_ERR_VALUE, "world must be in [1, 8] and rank in [0, world)");
+    if (!buffers) return fail(PD_ERR_VALUE, "buffers must not be NULL");
+    for (int s = 0; s < world; ++s)
+        if (!buffers[s] || (reinterpret_cast<uintptr_t>(buffers[s]) & 255))
+            return fail(PD_ERR_VALUE, "exchange buffers must be non-NULL and 256-byte aligned");
+    if (p->num_ctas > 1024) return fail(PD_ERR_VALUE, "exchange mode supports at most 1024 CTAs per rank");
+    if (total_ctas < p->num_ctas) return fail(PD_ERR_VALUE, "total_ctas must count every rank's CTAs");
+    DecodeArgs x{};
+    for (int s = 0; s < world; ++s) x.xpeer[s] = static_cast<uint8_t *>(buffers[s]);
+    x.xslot = exchange_slot_bytes(p);
+    x.xrank = rank;
+    x.xworld = world;
+    x.xtotal_ctas = total_ctas;
+    return decode_impl(p, q, k, v, dtype, out, stats, stream, nullptr, nullptr, &x);
+}

@@ -66,6 +66,18 @@ struct DecodeArgs {
     // or past it are skipped, and page ids always come from `table`.
     const int32_t *lengths;
     int32_t dynamic;
+    // Sequence-sharded exchange (xworld > 0).  Every final row of this rank
+    // (normalised o, m, l) goes to this rank's slot in every rank's exchange
+    // buffer, over NVLink; after all CTAs of all ranks have signalled, the
+    // CTAs merge the ranks' rows into `out` (and `stats`).  Buffer layout: u64
+    // arrival counter at +0, u32 launch count per CTA at +256, then two
+    // parities (alternate launches) of xworld slots of xslot bytes:
+    // [B*Hq*D o floats][B*Hq (m, l) pairs].
+    uint8_t *xpeer[8];
+    int64_t xslot;
+    int32_t xrank, xworld;
+    int32_t xtotal_ctas;          // CTAs of this launch over all ranks
+    int32_t rows;                 // B * Hq
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
 };
@@ -73,6 +85,14 @@ struct DecodeArgs {
 constexpr uint32_t kErrTimeout = 1u;
 constexpr uint32_t kErrBadPage = 2u;
 constexpr uint32_t kErrLength = 8u;
+constexpr int kMaxRanks = 8;
+constexpr int64_t kXEpochs = 256;     // u32 launch counts, one per CTA (up to 1024 CTAs)
+constexpr int64_t kXRecv = 256 + 4096;
+
+// Where this rank's rows go: slot `rank` of rank s's buffer, parity p.
+__device__ __forceinline__ float *xslot_of(const DecodeArgs &a, int s, int parity) {
+    return reinterpret_cast<float *>(a.xpeer[s] + kXRecv + (int64_t(parity) * a.xworld + a.xrank) * a.xslot);
+}
 
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS>
 struct KernelShape {
@@ -530,21 +550,37 @@ struct RowMerge {
     }
 
     // Normalised output (zero for an empty row) and, if asked, the (m, l) stats.
-    __device__ __forceinline__ void write(const DecodeArgs &a, int4 meta, int lane) const {
+    // Exchange mode (a.xworld > 0): the row goes to this rank's slot of every
+    // rank's exchange buffer (parity xpar) instead, with its (m, l).
+    __device__ __forceinline__ void write(const DecodeArgs &a, int4 meta, int lane, int xpar) const {
         const int c0 = LP > 1 ? lane % CH : lane;
         if (LP > 1 && lane >= CH) return;
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        float4 *dst = reinterpret_cast<float4 *>(a.out + int64_t(meta.x) * D);
+        float4 v[CPL];
 #pragma unroll
         for (int cc = 0; cc < CPL; ++cc)
-            dst[c0 + cc * 32] = make_float4(o[cc].x * inv, o[cc].y * inv, o[cc].z * inv, o[cc].w * inv);
+            v[cc] = make_float4(o[cc].x * inv, o[cc].y * inv, o[cc].z * inv, o[cc].w * inv);
+        if (a.xworld) {
+            for (int s = 0; s < a.xworld; ++s) {
+                float *slot = xslot_of(a, s, xpar);
+#pragma unroll
+                for (int cc = 0; cc < CPL; ++cc)
+                    reinterpret_cast<float4 *>(slot + int64_t(meta.x) * D)[c0 + cc * 32] = v[cc];
+                if (lane == 0)
+                    reinterpret_cast<float2 *>(slot + int64_t(a.rows) * D)[meta.x] = make_float2(m, l);
+            }
+            return;
+        }
+        float4 *dst = reinterpret_cast<float4 *>(a.out + int64_t(meta.x) * D);
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) dst[c0 + cc * 32] = v[cc];
         if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[meta.x] = make_float2(m, l);
     }
 };
 
 template <int D, int HG, int GT, int NSUB, int NC>
 __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *scratch, int warp, int lane,
-                                                int64_t lo, int rows, int team, int4 meta0) {
+                                                int64_t lo, int rows, int team, int4 meta0, int xpar) {
     using M = RowMerge<D, HG, GT, NSUB>;
     M rm;
     if (team == 1) {
@@ -552,7 +588,7 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
         for (int r = warp; r < rows; r += NC) {
             const int4 next = r + NC < rows ? __ldg(a.merge_rows + lo + r + NC) : meta;
             rm.fold(a, meta, 0, 1, lane);
-            rm.write(a, meta, lane);
+            rm.write(a, meta, lane, xpar);
             meta = next;
         }
         return;
@@ -581,7 +617,41 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
             rm.add(ml.x, ml.y, oo);
         }
-        rm.write(a, meta0, lane);
+        rm.write(a, meta0, lane, xpar);
+    }
+}
+
+// Exchange mode, after every rank's rows have landed: this CTA's share of the
+// output rows, each the max-corrected merge (oracle.py:88-96) of the ranks'
+// normalised rows o_s with weights 2^(m_s - M) l_s; zero when all are empty.
+// One warp per row, lanes over head dims; `stats` gets the merged (M, L).
+template <int D, int NC>
+__device__ __forceinline__ void merge_ranks(const DecodeArgs &a, int warp, int lane, int xpar) {
+    const int64_t R = a.rows;
+    const int64_t lo = R * blockIdx.x / gridDim.x, hi = R * (blockIdx.x + 1) / gridDim.x;
+    const float *slot0 = reinterpret_cast<const float *>(a.xpeer[a.xrank] + kXRecv + int64_t(xpar) * a.xworld * a.xslot);
+    const int64_t step = a.xslot / 4;   // floats from one rank's slot to the next
+    for (int64_t row = lo + warp; row < hi; row += NC) {
+        auto ml_of = [&](int s) { return __ldcv(reinterpret_cast<const float2 *>(slot0 + s * step + R * D) + row); };
+        float top = -INFINITY;
+        for (int s = 0; s < a.xworld; ++s) {
+            const float2 ml = ml_of(s);
+            if (ml.y > 0.f) top = fmaxf(top, ml.x);
+        }
+        float den = 0.f;
+        for (int s = 0; s < a.xworld; ++s) {
+            const float2 ml = ml_of(s);
+            if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
+        }
+        for (int d = lane; d < D; d += 32) {
+            float num = 0.f;
+            for (int s = 0; s < a.xworld; ++s) {
+                const float2 ml = ml_of(s);
+                if (ml.y > 0.f) num = fmaf(exp2f(ml.x - top) * ml.y, __ldcv(slot0 + s * step + row * D + d), num);
+            }
+            a.out[row * D + d] = den > 0.f ? num / den : 0.f;
+        }
+        if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
     }
 }
 
@@ -630,6 +700,10 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     // stream: everything above (plan metadata, shared-memory set-up) may
     // overlap its tail; q, the caches and every output wait for it to finish.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Exchange mode: this launch's number (1, 2, ...) and the buffer parity it writes.
+    const uint32_t xe = a.xworld
+        ? __ldcv(reinterpret_cast<const unsigned int *>(a.xpeer[a.xrank] + kXEpochs) + blockIdx.x) + 1u : 0u;
+    const int xpar = int(xe & 1u);
 
     if (warp == NC) {
         // ------------------------------------------------------------ producer
@@ -812,7 +886,18 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
 
             // ---------------------------------------------------- publish this warp's state
             eng.reduce();
-            if (sg.w < 0) {
+            if (sg.w < 0 && a.xworld) {
+                // the final row of this rank: to its slot in every rank's exchange buffer
+                for (int x = 0; x < a.xworld; ++x) {
+                    float *slot = xslot_of(a, x, xpar);
+                    eng.for_each_o([&](int g, int d, float o, float, float l) {
+                        if (g < nw) slot[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
+                    });
+                    eng.for_each_ml([&](int g, float m, float l) {
+                        if (g < nw) reinterpret_cast<float2 *>(slot + int64_t(a.rows) * D)[qhead0 + g] = make_float2(m, l);
+                    });
+                }
+            } else if (sg.w < 0) {
                 // the group's only segment and the only warp of this head: final output
                 eng.for_each_o([&](int g, int d, float o, float, float l) {
                     if (g < nw) a.out[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
@@ -851,9 +936,31 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             }
             named_barrier_sync(1, NC * 32);
             // After an abort a TMA load may still be landing in the ring: no merge.
-            if (!flags->abort) merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0);
-            return;
+            if (!flags->abort)
+                merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar);
         }
+        if (a.xworld) {
+            // All of this CTA's rows are in every rank's buffer: signal every
+            // rank (release at system scope), wait until all CTAs of all ranks
+            // have signalled this launch, then merge the ranks' rows.
+            named_barrier_sync(1, NC * 32);
+            if (warp == 0 && lane == 0) {
+                __threadfence_system();
+                for (int s = 0; s < a.xworld; ++s)
+                    atomicAdd_system(reinterpret_cast<unsigned long long *>(a.xpeer[s]), 1ull);
+                const unsigned long long target = (unsigned long long)xe * (unsigned long long)a.xtotal_ctas;
+                if (!wait_counter_sys(reinterpret_cast<const unsigned long long *>(a.xpeer[a.xrank]), target)) {
+                    atomicOr(a.error, kErrTimeout);
+                    flags->abort = 1;
+                }
+                __threadfence_system();
+                // this CTA's launch count, read back by the next launch
+                reinterpret_cast<uint32_t *>(a.xpeer[a.xrank] + kXEpochs)[blockIdx.x] = xe;
+            }
+            named_barrier_sync(1, NC * 32);
+            if (!flags->abort) merge_ranks<D, NC>(a, warp, lane, xpar);
+        }
+        if (a.fused_merge || a.xworld) return;
     }
     // Let the dependent merge kernel launch; it still waits for this grid to finish.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -117,6 +117,23 @@ __device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigne
     return true;
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until a counter that other GPUs add to (system-scope atomics over
+// NVLink) reaches `target`; false after the timeout.
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long *counter, unsigned long long target,
+                                                 unsigned long long timeout_ns = kWaitTimeoutNs) {
+    if (ld_acquire_sys_u64(counter) >= target) return true;
+    const unsigned long long start = global_ns();
+    while (ld_acquire_sys_u64(counter) < target)
+        if (global_ns() - start > timeout_ns) return false;
+    return true;
+}
+
 // ---------------------------------------------------------------- named barrier
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -49,6 +49,13 @@ SIGNATURES = {
     "pd_plan_bind": (_c_int32, [_vp, _vp, _c_size, _vp]),
     "pd_decode": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
     "pd_decode_dynamic": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp, _vp, _vp]),
+    "pd_exchange_bytes": (_c_size, [_vp, _c_int32]),
+    "pd_exchange_alloc": (_c_int32, [_c_int32, _c_size, ctypes.POINTER(_vp), _vp]),
+    "pd_exchange_open": (_c_int32, [_c_int32, _vp, ctypes.POINTER(_vp)]),
+    "pd_exchange_close": (_c_int32, [_c_int32, _vp]),
+    "pd_exchange_free": (_c_int32, [_c_int32, _vp]),
+    "pd_decode_exchange": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32,
+                                      _vp, _vp, _vp]),
     "pd_decode_with_stats": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),

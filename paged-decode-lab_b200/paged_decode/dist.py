@@ -10,13 +10,15 @@ natural ways:
   so there is no collective at all.
 
 * ``SequenceShardedPlan`` -- rank r owns a contiguous run of the logical pages
-  of every sequence (with those pages resident in its own cache).  It decodes
-  its run with ``run_with_stats`` into one packed FP32 buffer
-  ``[B*Hq*D outputs][B*Hq*2 (m, l)]``; the ranks all-gather the buffers and
-  every rank merges them with the max-corrected merge (``pd_merge_shards``),
-  the same algebra the reference uses across context partitions
-  (src/paged_decode/oracle.py:88-96).  NVLink bytes per step per rank:
-  (N-1) * B*Hq*(D+2)*4 received.
+  of every sequence (with those pages resident in its own cache).  Its rows
+  (normalised o, m, l per (b, h)) from all ranks are merged with the
+  max-corrected merge, the same algebra the reference uses across context
+  partitions (src/paged_decode/oracle.py:88-96).  By default one kernel per
+  rank does it all: decode, store the rows into every rank's exchange buffer
+  over NVLink, wait for the other ranks, merge (``pd_decode_exchange``).  The
+  alternative is ``run_with_stats`` + NCCL ``all_gather_into_tensor`` +
+  ``pd_merge_shards``.  NVLink bytes per step per rank: (N-1) * B*Hq*(D+2)*4
+  received.
 
 The pure functions (``kv_head_range``, ``query_head_range``,
 ``shard_sequence_metadata``, ``packed_size``) carry the sharding logic and are
@@ -140,44 +142,98 @@ class KVHeadShardedPlan:
 
 
 class SequenceShardedPlan:
-    """Sequence sharding: local split-K over this rank's pages, NCCL all-gather, merge.
+    """Sequence sharding: local split-K over this rank's pages, exchange, merge.
 
     ``table``/``lengths`` are this rank's local metadata (see
     ``shard_sequence_metadata``) over its own cache shard of ``physical_pages``
     pages.  ``run`` returns the full FP32 [B, Hq, D] output on every rank.
+
+    ``exchange="peer"`` (default, up to 8 ranks on one node): one kernel per
+    rank and step decodes, stores its rows into every rank's exchange buffer
+    over NVLink (CUDA IPC peer mappings, no multicast), waits for all ranks
+    (bounded) and merges (``pd_decode_exchange``).  ``exchange="nccl"``:
+    ``run_with_stats``, NCCL ``all_gather_into_tensor``, ``pd_merge_shards``.
+    Every rank must call ``run`` once per step; call ``close`` on every rank
+    (it synchronises them) before the process group goes away.
     """
 
     def __init__(self, layout: Layout, table, lengths, *, group=None, device="cuda",
-                 split_tokens=256, merge="serial", num_ctas=None):
+                 split_tokens=256, merge="serial", num_ctas=None, exchange="peer"):
         import torch
         import torch.distributed as dist
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.layout = layout
+        self.exchange = exchange
         table, lengths = validate_metadata(layout, table, lengths)
         self.plan = DecodePlan(layout, table, lengths, device=device, split_tokens=split_tokens,
                                merge=merge, num_ctas=num_ctas)
         self.device = self.plan.device
         rows = layout.batch * layout.query_heads
         self._rows = rows
-        self._send = torch.empty(packed_size(layout), dtype=torch.float32, device=self.device)
-        self._recv = torch.empty(self.world * packed_size(layout), dtype=torch.float32, device=self.device)
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim), dtype=torch.float32,
                                 device=self.device)
-        D = layout.head_dim
-        self._local_out = self._send[: rows * D].view(layout.batch, layout.query_heads, D)
-        self._local_stats = self._send[rows * D:].view(layout.batch, layout.query_heads, 2)
         self._lib = _native.load()
+        self._buffer = None
+        self._peers = []
+        if exchange == "peer":
+            if self.world > 8:
+                raise ValueError("peer exchange supports at most 8 ranks")
+            self._setup_peer()
+        else:
+            self._send = torch.empty(packed_size(layout), dtype=torch.float32, device=self.device)
+            self._recv = torch.empty(self.world * packed_size(layout), dtype=torch.float32,
+                                     device=self.device)
+            D = layout.head_dim
+            self._local_out = self._send[: rows * D].view(layout.batch, layout.query_heads, D)
+            self._local_stats = self._send[rows * D:].view(layout.batch, layout.query_heads, 2)
+
+    def _setup_peer(self):
+        import torch.distributed as dist
+        lib, dev = self._lib, self.device.index
+        # every rank's CTA count per input dtype, and one buffer per rank opened by all
+        counts = {code: int(p.info.num_ctas) for code, p in self.plan._native.items()}
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, counts, group=self.group)
+        self._total_ctas = {code: sum(g[code] for g in gathered) for code in counts}
+        nbytes = int(lib.pd_exchange_bytes(self.plan._native[_native.PD_FLOAT16].handle, self.world))
+        buffer, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        _native.check(lib.pd_exchange_alloc(dev, nbytes, ctypes.byref(buffer), handle), "exchange")
+        self._buffer = buffer
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=self.group)
+        ptrs = []
+        for s, h in enumerate(handles):
+            if s == self.rank:
+                ptrs.append(buffer.value)
+                continue
+            peer = ctypes.c_void_p()
+            _native.check(lib.pd_exchange_open(dev, ctypes.create_string_buffer(h, 64), ctypes.byref(peer)),
+                          "exchange")
+            self._peers.append(peer)
+            ptrs.append(peer.value)
+        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=self.group)
 
     @property
     def nvlink_bytes_per_step(self):
         """Bytes each rank receives from its peers per decode step."""
-        return (self.world - 1) * self._send.numel() * 4
+        return (self.world - 1) * packed_size(self.layout) * 4
 
     def run(self, q, k_local, v_local):
         import torch
         import torch.distributed as dist
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if self.exchange == "peer":
+            dtype = self.plan._check_inputs(q, k_local, v_local)
+            _native.check(self._lib.pd_decode_exchange(
+                self.plan._native[dtype].handle, q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), dtype,
+                self._ptrs, self.rank, self.world, self._total_ctas[dtype], self._out.data_ptr(), None,
+                stream), "decode")
+            return self._out
         self.plan.run_with_stats(q, k_local, v_local, self._local_out, self._local_stats)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
         D = self.layout.head_dim
@@ -185,5 +241,20 @@ class SequenceShardedPlan:
         base = self._recv.data_ptr()
         _native.check(self._lib.pd_merge_shards(
             base, base + self._rows * D * 4, self.world, stride, self._rows, D, self._out.data_ptr(),
-            torch.cuda.current_stream(self.device).cuda_stream), "merge_shards")
+            stream), "merge_shards")
         return self._out
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's, once every rank is done with them."""
+        import torch
+        import torch.distributed as dist
+        if self._buffer is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for peer in self._peers:
+            self._lib.pd_exchange_close(self.device.index, peer)
+        self._peers = []
+        dist.barrier(group=self.group)
+        self._lib.pd_exchange_free(self.device.index, self._buffer)
+        self._buffer = None

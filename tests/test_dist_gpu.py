@@ -57,8 +57,15 @@ def _worker(rank, world, port, q_out, mode):
             loc = Layout(3, 32, 8, 128, 32, max(1, len(ids)))
             idx = torch.as_tensor(ids, device=q.device)
             kl, vl = k[idx].contiguous(), v[idx].contiguous()
-            plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, device=f"cuda:{rank}")
-            out = plan.run(q, kl, vl).cpu().numpy()
+            exchange = "peer" if mode == "sequence_peer" else "nccl"
+            plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, device=f"cuda:{rank}", exchange=exchange)
+            first = plan.run(q, kl, vl).clone()
+            for _ in range(7):      # alternate exchange parities; every step the same bits
+                again = plan.run(q, kl, vl)
+                assert torch.equal(again, first)
+            out = first.cpu().numpy()
+            assert plan.plan.read_errors() == 0
+            plan.close()
             lo, hi = 0, 32
         torch.cuda.synchronize()
         ref = dense_attention(*(t.cpu().numpy() for t in (q, k, v)), table, lengths)[:, lo:hi]
@@ -71,7 +78,7 @@ def _worker(rank, world, port, q_out, mode):
         q_out.put((rank, False, f"{type(exc).__name__}: {exc}"))
 
 
-@pytest.mark.parametrize("mode", ["kv_head", "sequence"])
+@pytest.mark.parametrize("mode", ["kv_head", "sequence", "sequence_peer"])
 def test_two_gpu_sharding_matches_oracle(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

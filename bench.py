@@ -501,27 +501,36 @@ def run_ours(args, rank, local, world):
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, q, k, v, job.bytes_total, args.cpu_seconds)
-    if world == 1 and not args.no_competitors and w.dtype == "float16":
+    if world == 1 and not args.no_competitors:
         line["competitors"] = competitors(w, q, k, v, job, flush, args.steps)
     job.close()
     return line
 
 
 def competitors(w, q, k, v, job, flush, steps):
-    """FlashInfer's batch decode (the reference's measured competitor) on the same
-    caches, timed like our step; empty rows get one token (FlashInfer needs
-    nonempty contexts), so its workload is that much larger, never smaller."""
+    """The reference's comparisons on the same caches, timed like our step.
+
+    FlashInfer's batch decode (FP16 only; empty rows get one token because it
+    needs nonempty contexts, so its workload is that much larger, never
+    smaller) with and without its tensor-core path, and the dense baseline:
+    gather the pages into padded dense K/V and run PyTorch SDPA.
+    """
     import torch
-    from paged_decode.competitors import FlashInferPlan
+    from paged_decode.competitors import DenseSDPAPlan, FlashInferPlan
     table, lengths = w.table.copy(), w.lengths.copy()
     table[lengths == 0, 0] = 0
     lengths[lengths == 0] = 1
     out = {}
     ours = job.decode_plan.run(q, k, v).clone()
-    for tc in (False, True):
-        key = "flashinfer" + ("_tensor_cores" if tc else "")
+    live = torch.as_tensor(w.lengths > 0, device=q.device)   # rows the comparisons all define alike
+    entries = [("dense_gather_sdpa", lambda: DenseSDPAPlan(w.layout, w.table, w.lengths, device=q.device))]
+    if w.dtype == "float16":
+        entries += [("flashinfer", lambda: FlashInferPlan(w.layout, table, lengths, device=q.device)),
+                    ("flashinfer_tensor_cores",
+                     lambda: FlashInferPlan(w.layout, table, lengths, device=q.device, tensor_cores=True))]
+    for key, make in entries:
         try:
-            fi = FlashInferPlan(w.layout, table, lengths, device=q.device, tensor_cores=tc)
+            fi = make()
             for _ in range(3):
                 fi.run(q, k, v)
             torch.cuda.synchronize()
@@ -544,9 +553,11 @@ def competitors(w, q, k, v, job, flush, steps):
                     torch.cuda.synchronize()
                     times.append(a.elapsed_time(b))
                 ms = sum(times) / steps
-            out[key] = {"version": fi.version, "us_per_step": ms * 1e3,
+            result = fi.run(q, k, v)
+            torch.cuda.synchronize()
+            out[key] = {"version": getattr(fi, "version", torch.__version__), "us_per_step": ms * 1e3,
                         "value": job.bytes_total / (ms * 1e-3) / 1e12, "unit": "TB/s",
-                        "max_abs_vs_ours": float((fi.out.float() - ours).abs().max()),
+                        "max_abs_vs_ours": float((result.float() - ours)[live].abs().max()),
                         "timing": "same as value (back to back, or L2 flushed per step)"}
             del fi
         except Exception as exc:  # noqa: BLE001 - reported, never fatal

@@ -13,8 +13,11 @@ row b (padded with -1 to the longest row) and its length is
 
 ``FlashInferPlan`` runs FlashInfer's own batch decode on the same NHD caches,
 without copying them (the reference's measured competitor,
-competitors.py:21-62): comparison harness only, never on this package's
-decode path.
+competitors.py:21-62), and ``DenseSDPAPlan`` the dense baseline the reference
+reports (src/paged_decode/reference.py:7-46): gather the live pages into
+zero-padded [B, Hkv, L, D] tensors, then PyTorch's scaled_dot_product_attention
+with a length mask.  Comparison harness only, never on this package's decode
+path.
 """
 from __future__ import annotations
 
@@ -24,7 +27,7 @@ import numpy as np
 
 from .layout import Layout, validate_metadata
 
-__all__ = ["paged_csr", "csr_to_table", "FlashInferPlan"]
+__all__ = ["paged_csr", "csr_to_table", "FlashInferPlan", "DenseSDPAPlan"]
 
 
 def paged_csr(layout: Layout, table, lengths):
@@ -106,3 +109,38 @@ class FlashInferPlan:
         if q.dtype != torch.float16 or k.dtype != q.dtype or v.dtype != q.dtype:
             raise TypeError("FlashInfer comparison adapter requires FP16 inputs")
         return self.wrapper.run(q, (k, v), out=self.out)
+
+
+class DenseSDPAPlan:
+    """Gather the pages into dense K/V, then ``torch.nn.functional.scaled_dot_product_attention``.
+
+    The gather indices (physical page, slot) and the length mask are built
+    once; ``run`` does the gather (one indexed copy per cache) and the SDPA
+    call, both timed as the step.  Query heads share their KV head through
+    SDPA's GQA support, so the dense tensors are not repeated per query head.
+    All-empty rows come out as zeros (the reference's convention).
+    """
+
+    def __init__(self, layout: Layout, table, lengths, *, device="cuda"):
+        import torch
+        table, lengths = validate_metadata(layout, table, lengths)
+        self.layout = layout
+        span = max(1, int(lengths.max(initial=0)))
+        pos = np.arange(span)
+        live = pos[None, :] < lengths[:, None]
+        page_idx = np.where(live, pos[None, :] // layout.page_size, 0)
+        phys = np.take_along_axis(np.maximum(table, 0), page_idx, axis=1)
+        self.pages = torch.tensor(np.where(live, phys, 0), dtype=torch.long, device=device)
+        self.slots = torch.tensor(np.where(live, pos[None, :] % layout.page_size, 0), dtype=torch.long,
+                                  device=device)
+        self.mask = torch.tensor(live, device=device)[:, None, None, :]   # [B, 1, 1, L]
+        self.empty = torch.tensor(lengths == 0, device=device)[:, None, None]
+
+    def run(self, q, k, v):
+        import torch
+        import torch.nn.functional as F
+        dense_k = k[self.pages, self.slots].permute(0, 2, 1, 3)       # [B, Hkv, L, D]
+        dense_v = v[self.pages, self.slots].permute(0, 2, 1, 3)
+        out = F.scaled_dot_product_attention(q.unsqueeze(2), dense_k, dense_v, attn_mask=self.mask,
+                                             enable_gqa=True).squeeze(2)
+        return torch.where(self.empty, torch.zeros_like(out), out)

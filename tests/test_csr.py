@@ -66,3 +66,20 @@ def test_csr_to_table_random_and_empty_rows():
 def test_csr_to_table_rejects_bad_metadata(indptr, indices, last, error):
     with pytest.raises(error):
         csr_to_table(Layout(1, 4, 1, 64, 16, 4), np.array(indptr), np.array(indices), np.array(last))
+
+
+def test_dense_sdpa_baseline_matches_the_oracle_on_cpu():
+    """The dense comparison row (gather + PyTorch SDPA) computes the same attention."""
+    import torch
+    from oracle.paged_oracle import dense_attention
+    from paged_decode.competitors import DenseSDPAPlan
+    rng = np.random.default_rng(8)
+    layout = Layout(4, 8, 2, 64, 16, 20)
+    table = rng.permutation(20).reshape(4, 5).astype(np.int32)
+    lengths = np.array([0, 1, 33, 80], dtype=np.int32)
+    q = torch.randn(4, 8, 64, dtype=torch.float64)
+    k = torch.randn(20, 16, 2, 64, dtype=torch.float64)
+    v = torch.randn(20, 16, 2, 64, dtype=torch.float64)
+    out = DenseSDPAPlan(layout, table, lengths, device="cpu").run(q, k, v)
+    np.testing.assert_allclose(out.numpy(), dense_attention(q.numpy(), k.numpy(), v.numpy(), table, lengths),
+                               atol=1e-10, rtol=1e-10)

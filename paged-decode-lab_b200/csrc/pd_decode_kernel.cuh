@@ -109,7 +109,7 @@ struct KernelShape {
     static constexpr int THREADS = (NC + 1) * 32;
     static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
     // FP16 keeps each warp's 8 query heads in registers; FP32 stages them in
-    // the warp's own shared-memory slice.
+    // the warp's own shared-memory slice (no swizzle: lanes read whole rows).
     static constexpr bool Q_SMEM = ELT != 2;
     static constexpr size_t QS = Q_SMEM ? size_t(NC) * 8 * D * ELT : 0;
     static constexpr size_t BARS = size_t(SLOTS) * 16;
@@ -135,34 +135,30 @@ struct HalfEngine {
     static constexpr int KS = D / 16;    // k-steps of the QK^T product
     static constexpr int DT = D / 16;    // m-tiles of the PV product (head dims)
     static constexpr int MT = T / 16;    // 16-token m-tiles per page
-    static constexpr bool Q_REGS = NT <= 2;
+    static_assert(NT == 1, "a warp computes 8 query heads: one MMA n-tile");
 
-    uint32_t qf[Q_REGS ? KS : 1][Q_REGS ? NT : 1][2];
+    uint32_t qf[KS][NT][2];   // Q^T fragments of the warp's 8 query heads, in registers
     float acc[DT][NT][4];
     float m[NT][2], l[NT][2];
-    uint32_t qs;     // Q tile in shared memory (Q_REGS == false), row-swizzled
     int lane;
 
     // Q^T fragment: b0 = Q[g][d0..d0+1], b1 = Q[g][d0+8..d0+9], g = nt*8 + lane/4.
-    __device__ __forceinline__ void begin(const __half *qrow, int nh, int lane_, uint32_t qs_) {
+    __device__ __forceinline__ void begin(const __half *qrow, int nh, int lane_) {
         lane = lane_;
-        qs = qs_;
-        if constexpr (Q_REGS) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int g = nt * 8 + (lane >> 2);
+        for (int nt = 0; nt < NT; ++nt) {
+            const int g = nt * 8 + (lane >> 2);
 #pragma unroll
-                for (int ks = 0; ks < KS; ++ks) {
-                    const int d0 = ks * 16 + 2 * (lane & 3);
-                    uint32_t lo = 0, hi = 0;
-                    if (g < nh) {
-                        const uint32_t *src = reinterpret_cast<const uint32_t *>(qrow + g * D + d0);
-                        lo = src[0];
-                        hi = src[4];
-                    }
-                    qf[ks][nt][0] = lo;
-                    qf[ks][nt][1] = hi;
+            for (int ks = 0; ks < KS; ++ks) {
+                const int d0 = ks * 16 + 2 * (lane & 3);
+                uint32_t lo = 0, hi = 0;
+                if (g < nh) {
+                    const uint32_t *src = reinterpret_cast<const uint32_t *>(qrow + g * D + d0);
+                    lo = src[0];
+                    hi = src[4];
                 }
+                qf[ks][nt][0] = lo;
+                qf[ks][nt][1] = hi;
             }
         }
 #pragma unroll
@@ -179,22 +175,8 @@ struct HalfEngine {
     }
 
     __device__ __forceinline__ void q_frag(int ks, int nt, uint32_t &b0, uint32_t &b1) const {
-        if constexpr (Q_REGS) {
-            b0 = qf[ks][nt][0];
-            b1 = qf[ks][nt][1];
-        } else {
-            // rows g of 2*D bytes; 16-byte chunk c of row g stored at chunk (c ^ (g & 7)).
-            uint32_t r[2];
-            const int sub = (lane >> 3) & 1;     // lanes 0-7: chunk 2ks, lanes 8-15: chunk 2ks+1
-            const int g = nt * 8 + (lane & 7);
-            const int c = ks * 2 + sub;
-            const uint32_t addr = qs + g * (D * 2) + (((c & 8) | ((c & 7) ^ (g & 7))) << 4);
-            asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
-                         : "=r"(r[0]), "=r"(r[1])
-                         : "r"(addr));
-            b0 = r[0];
-            b1 = r[1];
-        }
+        b0 = qf[ks][nt][0];
+        b1 = qf[ks][nt][1];
     }
 
     __device__ __forceinline__ void tile(uint32_t kbase, uint32_t vbase, int valid, float scale_log2) {
@@ -843,23 +825,19 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             const Elt *qrow = static_cast<const Elt *>(a.q) + qhead0 * D;
             uint8_t *qmine = qsm + size_t(warp) * 8 * D * sizeof(Elt);
             const uint32_t qs = smem_u32(qmine);
-            static_assert(!std::is_same<Elt, __half>::value || HalfEngine<D, T, 8>::Q_REGS,
-                          "FP16 warps keep their 8 query heads in registers");
             if constexpr (S::Q_SMEM) {
-                // this warp's Q rows (zero rows for heads past nh) into its own slice
+                // FP32: this warp's Q rows (zero rows for heads past nh) into its own slice
                 constexpr int CPR = D * int(sizeof(Elt)) / 16;
                 for (int e = lane; e < 8 * CPR; e += 32) {
                     const int g = e / CPR, c = e % CPR;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (g < nw) v = __ldg(reinterpret_cast<const float4 *>(qrow + int64_t(g) * D) + c);
-                    // FP16 rows are read by ldmatrix: swizzle 16-byte chunks by row
-                    const int sc = std::is_same<Elt, __half>::value ? ((c & 8) | ((c & 7) ^ (g & 7))) : c;
-                    reinterpret_cast<float4 *>(qmine + size_t(g) * D * sizeof(Elt))[sc] = v;
+                    reinterpret_cast<float4 *>(qmine + size_t(g) * D * sizeof(Elt))[c] = v;
                 }
                 __syncwarp();
             }
             if constexpr (std::is_same<Elt, __half>::value)
-                eng.begin(reinterpret_cast<const __half *>(qrow), nw, lane, qs);
+                eng.begin(reinterpret_cast<const __half *>(qrow), nw, lane);
             else
                 eng.begin(nw, lane, qs);
 

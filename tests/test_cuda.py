@@ -404,3 +404,44 @@ def test_reference_kernel_agrees_on_the_same_inputs():
     ours = DecodePlan(layout, table, lengths).run(q, k, v).clone()
     theirs = ref_kernel.RefPlan(layout, table, lengths, device=q.device).run(q, k, v)
     torch.testing.assert_close(ours, theirs, atol=2e-3, rtol=1e-3)
+
+
+# ---------------------------------------------------------------- maximum sizes
+def _c_oracle(q, k, v, table, lengths):
+    from oracle.c_oracle import dense_attention as c_dense
+    return c_dense(*(t.cpu().numpy() for t in (q, k, v)), table, lengths)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_maximum_context_of_one_million_tokens(dtype):
+    """The reference's longest context (2^20 tokens, runtime.py:47) in one
+    sequence: 32768 pages of 32 tokens, beside a short and an empty one."""
+    page, width = 32, 32768
+    lengths = np.array([1 << 20, 77, 0], dtype=np.int32)
+    layout = Layout(3, 8, 1, 64, page, width + 3)
+    rng = np.random.default_rng(11)
+    table = np.full((3, width), -1, dtype=np.int32)
+    table[0] = rng.permutation(width + 3)[:width]
+    table[1, :3] = rng.choice(width + 3, 3, replace=False)
+    q, k, v = make_tensors(layout, dtype=dtype, seed=11)
+    plan = DecodePlan(layout, table, lengths)
+    assert plan.max_context == 1 << 20
+    out = plan.run(q, k, v).cpu().numpy()
+    tol = dict(atol=2e-3, rtol=1e-3) if dtype == torch.float16 else dict(atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(out, _c_oracle(q, k, v, table, lengths), **tol)
+    assert not out[2].any() and plan.read_errors() == 0
+
+
+def test_maximum_batch_of_65535_sequences():
+    """The reference's largest batch (65535, runtime.py:39), ragged lengths, one
+    page each at most, pages shared at random."""
+    batch = 65535
+    rng = np.random.default_rng(12)
+    lengths = rng.integers(0, 17, batch).astype(np.int32)
+    layout = Layout(batch, 4, 2, 128, 16, 4096)
+    table = rng.integers(0, 4096, (batch, 1)).astype(np.int32)
+    q, k, v = make_tensors(layout, seed=12)
+    plan = DecodePlan(layout, table, lengths)
+    out = plan.run(q, k, v).cpu().numpy()
+    np.testing.assert_allclose(out, _c_oracle(q, k, v, table, lengths), atol=2e-3, rtol=1e-3)
+    assert not out[lengths == 0].any() and plan.read_errors() == 0

@@ -923,9 +923,9 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             // have signalled this launch, then merge the ranks' rows.
             named_barrier_sync(1, NC * 32);
             if (warp == 0 && lane == 0) {
-                __threadfence_system();
+                fence_release_sys();
                 for (int s = 0; s < a.xworld; ++s)
-                    atomicAdd_system(reinterpret_cast<unsigned long long *>(a.xpeer[s]), 1ull);
+                    red_add_sys_u64(reinterpret_cast<unsigned long long *>(a.xpeer[s]), 1ull);
                 const unsigned long long target = (unsigned long long)xe * (unsigned long long)a.xtotal_ctas;
                 if (!wait_counter_sys(reinterpret_cast<const unsigned long long *>(a.xpeer[a.xrank]), target)) {
                     atomicOr(a.error, kErrTimeout);

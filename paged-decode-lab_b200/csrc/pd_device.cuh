@@ -117,6 +117,16 @@ __device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigne
     return true;
 }
 
+// One release fence at system scope, after which relaxed adds (no return
+// value, nothing to wait for) publish the caller's earlier writes.
+__device__ __forceinline__ void fence_release_sys() {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_add_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 3
+#define PD_ABI_VERSION 4
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -232,13 +232,14 @@ int32_t pd_abi_version(void);
  * other rank of the node with pd_exchange_open.  pd_decode_exchange decodes
  * this rank's pages (its plan covers its share of every sequence) and stores
  * each finished row (normalised o, m, l) into this rank's slot of every
- * rank's buffer, then signals every rank with a system-scope atomic, waits
- * (bounded, PD_DEVERR_TIMEOUT) until all `total_ctas` CTAs of all ranks have
- * signalled, and merges the ranks' rows into out (and stats when not NULL)
- * with the max-corrected merge.  Every rank must call it once per step, in
- * the same order, with buffers[s] = rank s's buffer as seen from this GPU
- * (buffers[rank] = its own); total_ctas = the sum of every rank's num_ctas
- * (<= 1024 each).  No multicast and no library kernel touches peer memory.
+ * rank's buffer over NVLink, tagging it with the launch number after a
+ * system-scope release fence.  Each output row is merged from the ranks'
+ * copies (max-corrected merge) into out (and stats when not NULL) as soon as
+ * all of them carry this launch's tag (bounded wait, PD_DEVERR_TIMEOUT).
+ * Every rank must call it once per step, in the same order, with buffers[s] =
+ * rank s's buffer as seen from this GPU (buffers[rank] = its own); at most
+ * 1024 CTAs per rank.  No multicast and no library kernel touches peer
+ * memory.
  */
 size_t pd_exchange_bytes(const pd_plan *plan, int32_t world);
 pd_status pd_exchange_alloc(int32_t device, size_t bytes, void **buffer, void *ipc_handle /* 64 bytes */);
@@ -246,8 +247,8 @@ pd_status pd_exchange_open(int32_t device, const void *ipc_handle, void **peer_b
 pd_status pd_exchange_close(int32_t device, void *peer_buffer);
 pd_status pd_exchange_free(int32_t device, void *buffer);
 pd_status pd_decode_exchange(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
-                             void *const *buffers, int32_t rank, int32_t world, int32_t total_ctas,
-                             float *out, float *stats, void *stream);
+                             void *const *buffers, int32_t rank, int32_t world, float *out, float *stats,
+                             void *stream);
 
 /* Diagnostics, no reference counterpart: runs the decode kernel's two kinds
  * of bounded wait against events that never happen -- an mbarrier phase that

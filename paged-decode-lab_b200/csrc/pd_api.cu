@@ -237,14 +237,14 @@ pd_status decode_impl(pd_plan *p, const void *q, const void *k, const void *v, p
         args.xslot = exchange->xslot;
         args.xrank = exchange->xrank;
         args.xworld = exchange->xworld;
-        args.xtotal_ctas = exchange->xtotal_ctas;
     }
     return launch(p, k, v, dtype, kModeDecode, args, stream);
 }
 
+// One rank's slot: rows * D o floats, then {m, l, tag, 0} per row.
 int64_t exchange_slot_bytes(const pd_plan *p) {
     const int64_t rows = int64_t(p->layout.batch) * p->layout.query_heads;
-    return (rows * (p->layout.head_dim + 2) * 4 + 255) / 256 * 256;
+    return (rows * (p->layout.head_dim + 4) * 4 + 255) / 256 * 256;
 }
 
 }  // namespace
@@ -563,8 +563,8 @@ PD_API pd_status pd_exchange_free(int32_t device, void *buffer) {
 }
 
 PD_API pd_status pd_decode_exchange(pd_plan *p, const void *q, const void *k, const void *v, pd_dtype dtype,
-                                    void *const *buffers, int32_t rank, int32_t world, int32_t total_ctas,
-                                    float *out, float *stats, void *stream) {
+                                    void *const *buffers, int32_t rank, int32_t world, float *out,
+                                    float *stats, void *stream) {
     if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
     if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
         return fail(PD_ERR_VALUE, "world must be in [1, 8] and rank in [0, world)");
@@ -573,12 +573,10 @@ PD_API pd_status pd_decode_exchange(pd_plan *p, const void *q, const void *k, co
         if (!buffers[s] || (reinterpret_cast<uintptr_t>(buffers[s]) & 255))
             return fail(PD_ERR_VALUE, "exchange buffers must be non-NULL and 256-byte aligned");
     if (p->num_ctas > 1024) return fail(PD_ERR_VALUE, "exchange mode supports at most 1024 CTAs per rank");
-    if (total_ctas < p->num_ctas) return fail(PD_ERR_VALUE, "total_ctas must count every rank's CTAs");
     DecodeArgs x{};
     for (int s = 0; s < world; ++s) x.xpeer[s] = static_cast<uint8_t *>(buffers[s]);
     x.xslot = exchange_slot_bytes(p);
     x.xrank = rank;
     x.xworld = world;
-    x.xtotal_ctas = total_ctas;
     return decode_impl(p, q, k, v, dtype, out, stats, stream, nullptr, nullptr, &x);
 }

@@ -67,16 +67,16 @@ struct DecodeArgs {
     const int32_t *lengths;
     int32_t dynamic;
     // Sequence-sharded exchange (xworld > 0).  Every final row of this rank
-    // (normalised o, m, l) goes to this rank's slot in every rank's exchange
-    // buffer, over NVLink; after all CTAs of all ranks have signalled, the
-    // CTAs merge the ranks' rows into `out` (and `stats`).  Buffer layout: u64
-    // arrival counter at +0, u32 launch count per CTA at +256, then two
-    // parities (alternate launches) of xworld slots of xslot bytes:
-    // [B*Hq*D o floats][B*Hq (m, l) pairs].
+    // (normalised o, then (m, l)) goes to this rank's slot in every rank's
+    // exchange buffer over NVLink, followed (after a system-scope release
+    // fence) by the row's tag: this launch's number.  A row of `out` is merged
+    // from the ranks' rows once all of their tags show this launch.  Buffer
+    // layout: u32 launch count per CTA at +256, then two parities (alternate
+    // launches) of xworld slots of xslot bytes: [B*Hq*D o floats][B*Hq x
+    // {m, l, tag, 0}].
     uint8_t *xpeer[8];
     int64_t xslot;
     int32_t xrank, xworld;
-    int32_t xtotal_ctas;          // CTAs of this launch over all ranks
     int32_t rows;                 // B * Hq
     int64_t P;
     float scale_log2;         // log2(e) / sqrt(D)
@@ -92,6 +92,39 @@ constexpr int64_t kXRecv = 256 + 4096;
 // Where this rank's rows go: slot `rank` of rank s's buffer, parity p.
 __device__ __forceinline__ float *xslot_of(const DecodeArgs &a, int s, int parity) {
     return reinterpret_cast<float *>(a.xpeer[s] + kXRecv + (int64_t(parity) * a.xworld + a.xrank) * a.xslot);
+}
+
+// {m, l, tag, 0} of `row` in a slot (after the slot's rows * D o floats).
+template <int D>
+__device__ __forceinline__ float4 *xmeta_of(float *slot, const DecodeArgs &a, int64_t row) {
+    return reinterpret_cast<float4 *>(slot + int64_t(a.rows) * D) + row;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u32(unsigned *p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// After a warp stored rows rows0 .. rows0 + n - 1 (o and (m, l)) into every
+// rank's slot: release them, then tag each with this launch's number.
+template <int D>
+__device__ __forceinline__ void publish_rows(const DecodeArgs &a, int64_t row0, int n, int xpar, unsigned xe,
+                                             int lane) {
+    __syncwarp();
+    if (lane == 0 && n > 0) {
+        fence_release_sys();
+        for (int s = 0; s < a.xworld; ++s) {
+            float *slot = xslot_of(a, s, xpar);
+            for (int i = 0; i < n; ++i)
+                st_relaxed_sys_u32(reinterpret_cast<unsigned *>(&xmeta_of<D>(slot, a, row0 + i)->z), xe);
+        }
+    }
+    __syncwarp();
 }
 
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS>
@@ -548,8 +581,7 @@ struct RowMerge {
 #pragma unroll
                 for (int cc = 0; cc < CPL; ++cc)
                     reinterpret_cast<float4 *>(slot + int64_t(meta.x) * D)[c0 + cc * 32] = v[cc];
-                if (lane == 0)
-                    reinterpret_cast<float2 *>(slot + int64_t(a.rows) * D)[meta.x] = make_float2(m, l);
+                if (lane == 0) *reinterpret_cast<float2 *>(xmeta_of<D>(slot, a, meta.x)) = make_float2(m, l);
             }
             return;
         }
@@ -562,7 +594,8 @@ struct RowMerge {
 
 template <int D, int HG, int GT, int NSUB, int NC>
 __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *scratch, int warp, int lane,
-                                                int64_t lo, int rows, int team, int4 meta0, int xpar) {
+                                                int64_t lo, int rows, int team, int4 meta0, int xpar,
+                                                unsigned xe) {
     using M = RowMerge<D, HG, GT, NSUB>;
     M rm;
     if (team == 1) {
@@ -571,6 +604,7 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
             const int4 next = r + NC < rows ? __ldg(a.merge_rows + lo + r + NC) : meta;
             rm.fold(a, meta, 0, 1, lane);
             rm.write(a, meta, lane, xpar);
+            if (a.xworld) publish_rows<D>(a, meta.x, 1, xpar, xe, lane);
             meta = next;
         }
         return;
@@ -600,39 +634,74 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
             rm.add(ml.x, ml.y, oo);
         }
         rm.write(a, meta0, lane, xpar);
+        if (a.xworld) publish_rows<D>(a, meta0.x, 1, xpar, xe, lane);
     }
 }
 
-// Exchange mode, after every rank's rows have landed: this CTA's share of the
-// output rows, each the max-corrected merge (oracle.py:88-96) of the ranks'
-// normalised rows o_s with weights 2^(m_s - M) l_s; zero when all are empty.
-// One warp per row, lanes over head dims; `stats` gets the merged (M, L).
+// Exchange mode: this CTA's share of the output rows, each merged as soon as
+// every rank's copy of it carries this launch's tag: the max-corrected merge
+// (oracle.py:88-96) of the ranks' normalised rows o_s with weights
+// 2^(m_s - M) l_s; zero when all are empty.  One warp per row: lane s polls
+// rank s's tag, then every (m, l) and every lane's o chunk of all ranks load
+// together; `stats` gets the merged (M, L).
 template <int D, int NC>
-__device__ __forceinline__ void merge_ranks(const DecodeArgs &a, int warp, int lane, int xpar) {
+__device__ __forceinline__ void merge_ranks(const DecodeArgs &a, int warp, int lane, int xpar, unsigned xe) {
+    constexpr int CH = D / 4;
     const int64_t R = a.rows;
     const int64_t lo = R * blockIdx.x / gridDim.x, hi = R * (blockIdx.x + 1) / gridDim.x;
-    const float *slot0 = reinterpret_cast<const float *>(a.xpeer[a.xrank] + kXRecv + int64_t(xpar) * a.xworld * a.xslot);
+    float *slot0 = reinterpret_cast<float *>(a.xpeer[a.xrank] + kXRecv + int64_t(xpar) * a.xworld * a.xslot);
     const int64_t step = a.xslot / 4;   // floats from one rank's slot to the next
     for (int64_t row = lo + warp; row < hi; row += NC) {
-        auto ml_of = [&](int s) { return __ldcv(reinterpret_cast<const float2 *>(slot0 + s * step + R * D) + row); };
-        float top = -INFINITY;
-        for (int s = 0; s < a.xworld; ++s) {
-            const float2 ml = ml_of(s);
-            if (ml.y > 0.f) top = fmaxf(top, ml.x);
-        }
-        float den = 0.f;
-        for (int s = 0; s < a.xworld; ++s) {
-            const float2 ml = ml_of(s);
-            if (ml.y > 0.f) den = fmaf(exp2f(ml.x - top), ml.y, den);
-        }
-        for (int d = lane; d < D; d += 32) {
-            float num = 0.f;
-            for (int s = 0; s < a.xworld; ++s) {
-                const float2 ml = ml_of(s);
-                if (ml.y > 0.f) num = fmaf(exp2f(ml.x - top) * ml.y, __ldcv(slot0 + s * step + row * D + d), num);
+        bool ok = true;
+        if (lane < a.xworld) {
+            const unsigned *tag =
+                reinterpret_cast<const unsigned *>(&xmeta_of<D>(slot0 + lane * step, a, row)->z);
+            if (ld_acquire_sys_u32(tag) < xe) {
+                const unsigned long long start = global_ns();
+                while (ld_acquire_sys_u32(tag) < xe)
+                    if (global_ns() - start > kWaitTimeoutNs) {
+                        ok = false;
+                        break;
+                    }
             }
-            a.out[row * D + d] = den > 0.f ? num / den : 0.f;
         }
+        ok = __all_sync(kFullMask, ok);
+        __syncwarp();
+        if (!ok) {
+            if (lane == 0) atomicOr(a.error, kErrTimeout);
+            continue;
+        }
+        float2 ml[kMaxRanks];
+        float4 v[kMaxRanks];
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s) {
+            ml[s] = make_float2(-INFINITY, 0.f);
+            v[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (s < a.xworld) {
+                ml[s] = __ldcv(reinterpret_cast<const float2 *>(xmeta_of<D>(slot0 + s * step, a, row)));
+                if (lane < CH) v[s] = __ldcv(reinterpret_cast<const float4 *>(slot0 + s * step + row * D) + lane);
+            }
+        }
+        float top = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+            if (ml[s].y > 0.f) top = fmaxf(top, ml[s].x);
+        float den = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+            if (ml[s].y > 0.f) {
+                const float w = exp2f(ml[s].x - top) * ml[s].y;
+                den += w;
+                acc.x = fmaf(w, v[s].x, acc.x);
+                acc.y = fmaf(w, v[s].y, acc.y);
+                acc.z = fmaf(w, v[s].z, acc.z);
+                acc.w = fmaf(w, v[s].w, acc.w);
+            }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        if (lane < CH)
+            reinterpret_cast<float4 *>(a.out + row * D)[lane] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         if (a.stats && lane == 0) reinterpret_cast<float2 *>(a.stats)[row] = make_float2(top, den);
     }
 }
@@ -872,9 +941,10 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                         if (g < nw) slot[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
                     });
                     eng.for_each_ml([&](int g, float m, float l) {
-                        if (g < nw) reinterpret_cast<float2 *>(slot + int64_t(a.rows) * D)[qhead0 + g] = make_float2(m, l);
+                        if (g < nw) *reinterpret_cast<float2 *>(xmeta_of<D>(slot, a, qhead0 + g)) = make_float2(m, l);
                     });
                 }
+                publish_rows<D>(a, qhead0, max(nw, 0), xpar, xe, lane);
             } else if (sg.w < 0) {
                 // the group's only segment and the only warp of this head: final output
                 eng.for_each_o([&](int g, int d, float o, float, float l) {
@@ -915,28 +985,14 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             named_barrier_sync(1, NC * 32);
             // After an abort a TMA load may still be landing in the ring: no merge.
             if (!flags->abort)
-                merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar);
+                merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
         }
         if (a.xworld) {
-            // All of this CTA's rows are in every rank's buffer: signal every
-            // rank (release at system scope), wait until all CTAs of all ranks
-            // have signalled this launch, then merge the ranks' rows.
-            named_barrier_sync(1, NC * 32);
-            if (warp == 0 && lane == 0) {
-                fence_release_sys();
-                for (int s = 0; s < a.xworld; ++s)
-                    red_add_sys_u64(reinterpret_cast<unsigned long long *>(a.xpeer[s]), 1ull);
-                const unsigned long long target = (unsigned long long)xe * (unsigned long long)a.xtotal_ctas;
-                if (!wait_counter_sys(reinterpret_cast<const unsigned long long *>(a.xpeer[a.xrank]), target)) {
-                    atomicOr(a.error, kErrTimeout);
-                    flags->abort = 1;
-                }
-                __threadfence_system();
-                // this CTA's launch count, read back by the next launch
+            // This CTA's rows are published (tagged) as they are written; merge
+            // this CTA's share of the output rows as the ranks' copies arrive.
+            if (warp == 0 && lane == 0)   // this CTA's launch count, read back by the next launch
                 reinterpret_cast<uint32_t *>(a.xpeer[a.xrank] + kXEpochs)[blockIdx.x] = xe;
-            }
-            named_barrier_sync(1, NC * 32);
-            if (!flags->abort) merge_ranks<D, NC>(a, warp, lane, xpar);
+            if (!flags->abort) merge_ranks<D, NC>(a, warp, lane, xpar, xe);
         }
         if (a.fused_merge || a.xworld) return;
     }

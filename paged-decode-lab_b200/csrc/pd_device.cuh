@@ -117,31 +117,10 @@ __device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigne
     return true;
 }
 
-// One release fence at system scope, after which relaxed adds (no return
-// value, nothing to wait for) publish the caller's earlier writes.
+// Release at system scope: the caller's earlier writes (and those it has
+// synchronised with) become visible to other GPUs before its later stores.
 __device__ __forceinline__ void fence_release_sys() {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-}
-
-__device__ __forceinline__ void red_add_sys_u64(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Wait until a counter that other GPUs add to (system-scope atomics over
-// NVLink) reaches `target`; false after the timeout.
-__device__ __forceinline__ bool wait_counter_sys(const unsigned long long *counter, unsigned long long target,
-                                                 unsigned long long timeout_ns = kWaitTimeoutNs) {
-    if (ld_acquire_sys_u64(counter) >= target) return true;
-    const unsigned long long start = global_ns();
-    while (ld_acquire_sys_u64(counter) < target)
-        if (global_ns() - start > timeout_ns) return false;
-    return true;
 }
 
 // ---------------------------------------------------------------- named barrier

@@ -54,8 +54,7 @@ SIGNATURES = {
     "pd_exchange_open": (_c_int32, [_c_int32, _vp, ctypes.POINTER(_vp)]),
     "pd_exchange_close": (_c_int32, [_c_int32, _vp]),
     "pd_exchange_free": (_c_int32, [_c_int32, _vp]),
-    "pd_decode_exchange": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _c_int32,
-                                      _vp, _vp, _vp]),
+    "pd_decode_exchange": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _c_int32, _c_int32, _vp, _vp, _vp]),
     "pd_decode_with_stats": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
@@ -84,7 +83,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 3:
+        if lib.pd_abi_version() != 4:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

@@ -150,8 +150,9 @@ class SequenceShardedPlan:
 
     ``exchange="peer"`` (default, up to 8 ranks on one node): one kernel per
     rank and step decodes, stores its rows into every rank's exchange buffer
-    over NVLink (CUDA IPC peer mappings, no multicast), waits for all ranks
-    (bounded) and merges (``pd_decode_exchange``).  ``exchange="nccl"``:
+    over NVLink (CUDA IPC peer mappings, no multicast) with a per-row launch
+    tag, and merges each output row once every rank's copy of it has arrived
+    (bounded wait; ``pd_decode_exchange``).  ``exchange="nccl"``:
     ``run_with_stats``, NCCL ``all_gather_into_tensor``, ``pd_merge_shards``.
     Every rank must call ``run`` once per step; call ``close`` on every rank
     (it synchronises them) before the process group goes away.
@@ -194,11 +195,7 @@ class SequenceShardedPlan:
     def _setup_peer(self):
         import torch.distributed as dist
         lib, dev = self._lib, self.device.index
-        # every rank's CTA count per input dtype, and one buffer per rank opened by all
-        counts = {code: int(p.info.num_ctas) for code, p in self.plan._native.items()}
-        gathered = [None] * self.world
-        dist.all_gather_object(gathered, counts, group=self.group)
-        self._total_ctas = {code: sum(g[code] for g in gathered) for code in counts}
+        # one buffer per rank, opened by every other rank
         nbytes = int(lib.pd_exchange_bytes(self.plan._native[_native.PD_FLOAT16].handle, self.world))
         buffer, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
         _native.check(lib.pd_exchange_alloc(dev, nbytes, ctypes.byref(buffer), handle), "exchange")
@@ -231,8 +228,7 @@ class SequenceShardedPlan:
             dtype = self.plan._check_inputs(q, k_local, v_local)
             _native.check(self._lib.pd_decode_exchange(
                 self.plan._native[dtype].handle, q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), dtype,
-                self._ptrs, self.rank, self.world, self._total_ctas[dtype], self._out.data_ptr(), None,
-                stream), "decode")
+                self._ptrs, self.rank, self.world, self._out.data_ptr(), None, stream), "decode")
             return self._out
         self.plan.run_with_stats(q, k_local, v_local, self._local_out, self._local_stats)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)

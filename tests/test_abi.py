@@ -104,3 +104,37 @@ def test_exception_mapping():
         _native.check(_native.PD_ERR_CUDA)
     with pytest.raises(RuntimeError):
         _native.check(_native.PD_ERR_UNBOUND)
+
+
+def test_header_is_plain_c_and_links_from_c(tmp_path):
+    """A C99 caller compiles against include/paged_decode.h, links the library
+    and calls it (no GPU needed for the ABI version)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "caller.c"
+    src.write_text('#include "paged_decode.h"\n'
+                   "int main(void) { return pd_abi_version() == PD_ABI_VERSION ? 0 : 1; }\n")
+    lib = Path(_native.LIB_PATH)
+    exe = tmp_path / "caller"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-pedantic", f"-I{HEADER.parent}", str(src),
+                    str(lib), f"-Wl,-rpath,{lib.parent}", "-o", str(exe)], check=True)
+    subprocess.run([str(exe)], check=True)
+
+
+def test_exchange_buffer_size():
+    """pd_exchange_bytes: launch counts (4 KiB after 256 B), then two parities of
+    `world` slots of B*Hq*(D + 4) floats rounded up to 256 bytes."""
+    lib = _native.load()
+    layout = (3, 8, 2, 64, 16, 6)
+    status, handle = _create(layout, np.arange(6, dtype=np.int32).reshape(3, 2), [17, 0, 32])
+    assert status == 0
+    try:
+        slot = -(-(3 * 8 * (64 + 4) * 4) // 256) * 256
+        for world in (1, 2, 8):
+            assert lib.pd_exchange_bytes(handle, world) == 256 + 4096 + 2 * world * slot
+        assert lib.pd_exchange_bytes(handle, 9) == 0 and lib.pd_exchange_bytes(None, 2) == 0
+    finally:
+        lib.pd_plan_destroy(handle)

@@ -50,7 +50,7 @@ def check_worklist(layout, table, lengths, plan):
     cpt = hg * gt // 8
     assert cpt <= 8
     tile = 2 * layout.head_dim * 2 * T * hg
-    want = 1 if tile >= 32768 else min(2 if tile >= 16384 else 4, 8 // cpt)
+    want = 1 if tile >= 32768 else min(4, 8 // cpt)
     assert stride == max(1, want)
     covered = {gi: [] for gi in range(len(groups))}
     for c in range(C):

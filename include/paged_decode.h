@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 4
+#define PD_ABI_VERSION 5
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -219,6 +219,30 @@ size_t pd_static_scratch_capacity(void);
 /* Copy the device error word to *error_word and clear it (synchronises `stream`). */
 pd_status pd_plan_read_errors(pd_plan *plan, uint32_t *error_word, void *stream);
 
+/* How a plan whose split rows are merged inside the decode kernel (pd_plan_info
+ * merge_in_kernel) launches the grid barrier before the merge.  No reference
+ * counterpart (the reference always merges with a second kernel).
+ *   PD_BARRIER_PLAIN (default): a plain launch, so that it can start on SMs as
+ *     the previous kernel's CTAs leave them.  Nothing then promises that all
+ *     CTAs are resident together (an SM partition, a kernel in another stream),
+ *     so a CTA that has waited at the barrier for 50 us while some CTA of the
+ *     launch has not yet started leaves, and the CTA that completes the barrier
+ *     merges the rows of those that left.  Same results, bit for bit.
+ *   PD_BARRIER_COOPERATIVE: a cooperative launch: all CTAs resident, or it is
+ *     refused and the separate merge kernel runs instead.
+ *   PD_BARRIER_LEAVE_AT_ONCE: a plain launch in which every CTA that has to
+ *     wait leaves at once (exercises the fallback; for tests).
+ * Exchange launches (pd_decode_exchange) are always cooperative. */
+#define PD_BARRIER_PLAIN 0
+#define PD_BARRIER_COOPERATIVE 1
+#define PD_BARRIER_LEAVE_AT_ONCE 2
+pd_status pd_plan_set_barrier(pd_plan *plan, int32_t mode);
+
+/* Launches since the last call whose barrier fell back to merging the rows of
+ * CTAs that left; copies the count to *count and clears it (synchronises
+ * `stream`). */
+pd_status pd_plan_read_barrier_fallbacks(pd_plan *plan, uint32_t *count, void *stream);
+
 const char *pd_status_string(pd_status status);
 const char *pd_last_error(void);     /* message of this thread's last failing call */
 int32_t pd_abi_version(void);
@@ -258,6 +282,15 @@ pd_status pd_decode_exchange(pd_plan *plan, const void *q, const void *k, const 
  * without a fault or a hang; synchronous on the default stream of `device`.
  */
 pd_status pd_selftest_wait_timeouts(int32_t device, uint32_t timeout_us, uint32_t *words);
+
+/* Diagnostics, no reference counterpart: one CTA reaches a grid barrier for two
+ * CTAs in PD_BARRIER_PLAIN's leave mode, with leave_us (1 .. 1e5) as the wait
+ * before leaving.  outcomes[0]: the partner has not started -- the CTA leaves
+ * (2); outcomes[1]: the number of CTAs that left, as recorded in the barrier's
+ * count (1); outcomes[2]: the CTA's left bit (1); outcomes[3]: the partner has
+ * started but never arrives -- the CTA must stay, and times out after
+ * 4 * leave_us (3).  Synchronous on the default stream of `device`. */
+pd_status pd_selftest_barrier_leave(int32_t device, uint32_t leave_us, uint32_t *outcomes);
 
 #ifdef __cplusplus
 }

@@ -137,7 +137,12 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.group = p->group;
     a.slot_stride = p->slot_stride;
     a.num_groups = int32_t(p->groups.size() / 8);
-    a.ticket = reinterpret_cast<unsigned long long *>(dev + im.off_error + 8);
+    a.gb.count = reinterpret_cast<unsigned long long *>(dev + im.off_error + 8);
+    a.gb.started = reinterpret_cast<unsigned long long *>(dev + im.off_error + 16);
+    a.gb.left = reinterpret_cast<unsigned long long *>(dev + im.off_error + 64);
+    a.gb.leave_mode = 0;
+    a.gb.leave_ns = kBarrierLeaveNs;
+    a.fallbacks = reinterpret_cast<uint32_t *>(dev + im.off_error + 4);
     a.merge_rows = reinterpret_cast<const int4 *>(dev + im.off_merge);
     a.num_merge_rows = int32_t(p->merge_rows.size() / 4);
     a.fused_merge = p->merge_in_kernel ? 1 : 0;
@@ -191,7 +196,25 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     attr[1].val.cooperative = 1;
     cfg.attrs = attr;
     cudaError_t err;
-    if (la.fused_merge || la.xworld) {
+    if (la.fused_merge && !la.xworld && p->barrier_mode != PD_BARRIER_COOPERATIVE) {
+        // A plain launch starts on SMs as the previous kernel's CTAs leave
+        // them (measured 2-3 us a step ahead of a cooperative launch).  The
+        // grid barrier then lets a CTA leave when another has not started, so
+        // residency is not required; the CTAs must merely fit the GPU at once.
+        if (p->occ_fn != reinterpret_cast<const void *>(e.fn)) {
+            int per_sm = 0;
+            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e.fn, e.threads, e.smem);
+            if (err != cudaSuccess)
+                return fail(PD_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(err));
+            p->occ_fn = reinterpret_cast<const void *>(e.fn);
+            p->occ_ctas = per_sm * p->sm_count;
+        }
+        if (p->num_ctas <= p->occ_ctas) {
+            la.gb.leave_mode = p->barrier_mode == PD_BARRIER_LEAVE_AT_ONCE ? 2u : 1u;
+        } else {
+            la.fused_merge = 0;
+        }
+    } else if (la.fused_merge || la.xworld) {
         // The CTAs wait for each other at a grid barrier before merging, and
         // in exchange mode for every CTA of every rank; a cooperative launch
         // guarantees they are all resident, or refuses.
@@ -207,7 +230,7 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     err = cudaLaunchKernelEx(&cfg, e.fn, tc.map_k, tc.map_v, la);
     if (err != cudaSuccess)
         return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
-    if (mode == kModeDecode && p->num_pieces > 0) {
+    if (mode == kModeDecode && p->num_pieces > 0 && !la.fused_merge) {
         err = launch_merge_partials(la, p->heads_per_tile, p->group_tile, e.nsub, p->layout.head_dim, st);
         if (err != cudaSuccess)
             return fail(PD_ERR_CUDA, std::string("merge launch: ") + cudaGetErrorString(err));
@@ -474,6 +497,30 @@ PD_API pd_status pd_gather_debug(pd_plan *p, const void *k, const void *v, pd_dt
     args.dense_k = dense_k;
     args.dense_v = dense_v;
     return launch(p, k, v, dtype, kModeGather, args, stream);
+}
+
+PD_API pd_status pd_plan_set_barrier(pd_plan *p, int32_t mode) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    if (mode != PD_BARRIER_PLAIN && mode != PD_BARRIER_COOPERATIVE && mode != PD_BARRIER_LEAVE_AT_ONCE)
+        return fail(PD_ERR_VALUE, "barrier mode must be PD_BARRIER_PLAIN, _COOPERATIVE or _LEAVE_AT_ONCE");
+    p->barrier_mode = mode;
+    return PD_OK;
+}
+
+PD_API pd_status pd_plan_read_barrier_fallbacks(pd_plan *p, uint32_t *count, void *stream) {
+    pd_status s = check_bound(p);
+    if (s != PD_OK) return s;
+    if (!count) return fail(PD_ERR_VALUE, "count must not be NULL");
+    DeviceGuard guard(p->device);
+    auto st = static_cast<cudaStream_t>(stream);
+    uint32_t word = 0;
+    cudaError_t err = cudaMemcpyAsync(&word, p->dev + p->image.off_error + 4, 4, cudaMemcpyDeviceToHost, st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(p->dev + p->image.off_error + 4, 0, 4, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("fallback count read: ") + cudaGetErrorString(err));
+    *count = word;
+    return PD_OK;
 }
 
 PD_API pd_status pd_plan_read_errors(pd_plan *p, uint32_t *error_word, void *stream) {

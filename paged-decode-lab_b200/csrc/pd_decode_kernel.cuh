@@ -56,8 +56,9 @@ struct DecodeArgs {
     int32_t Hq, Hkv, W, max_len, group;   // group = G = Hq / Hkv
     int32_t slot_stride;      // partial slots reserved per segment (>= NSUB)
     int32_t num_groups;
-    // in-kernel merge (cooperative launch): grid barrier ticket and the rows to merge
-    unsigned long long *ticket;
+    // in-kernel merge: the grid barrier (its counters live in the plan) and the rows to merge
+    GridBarrier gb;
+    uint32_t *fallbacks;         // launches whose last CTA merged the shares of CTAs that left
     const int4 *merge_rows;      // split groups' rows: {out row, slot0, segments, head * GT + query head}
     int32_t num_merge_rows;
     int32_t fused_merge;         // 1: the CTAs merge the partials after a grid barrier
@@ -152,7 +153,8 @@ struct KernelShape {
 
 struct SmemFlags {
     volatile int abort;
-    int pad[3];
+    int barrier;        // grid_arrive's outcome (kBarrier*)
+    int pad[2];
 };
 
 // ------------------------------------------------------------------ FP16 tensor-core engine
@@ -482,7 +484,7 @@ struct EngineFor<float, D, T, GT> {
 enum : int { kModeDecode = 0, kModeGather = 1 };
 
 // ------------------------------------------------------------------ in-kernel merge
-// Runs in every CTA after the grid barrier of a cooperative launch, in place
+// Runs in every CTA after the grid barrier (grid_arrive), in place
 // of the separate merge kernel.  The split groups' output rows (merge_rows,
 // {out row, first slot, segments, column}) are cut into gridDim.x contiguous
 // shares.  With at least NC rows a warp takes every NC-th row of its CTA's
@@ -751,6 +753,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     // stream: everything above (plan metadata, shared-memory set-up) may
     // overlap its tail; q, the caches and every output wait for it to finish.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (MODE == kModeDecode && a.fused_merge && threadIdx.x == 0) atomicAdd(a.gb.started, 1ull);
     // Exchange mode: this launch's number (1, 2, ...) and the buffer parity it writes.
     const uint32_t xe = a.xworld
         ? __ldcv(reinterpret_cast<const unsigned int *>(a.xpeer[a.xrank] + kXEpochs) + blockIdx.x) + 1u : 0u;
@@ -967,25 +970,60 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     }
     if constexpr (MODE == kModeDecode) {
         if (a.fused_merge) {
-            static_assert(size_t(NC) * (D * 4 + 8) <= S::RING, "merge scratch must fit in the ring");
-            // this CTA's share of the merge rows; each warp's first row loads
-            // while the CTAs gather at the barrier
+            // merge scratch, then a snapshot of the left-CTA bits (1024 bits)
+            static_assert(size_t(NC) * (D * 4 + 8) + 128 <= S::RING, "merge scratch must fit in the ring");
+            unsigned long long *left_snap =
+                reinterpret_cast<unsigned long long *>(ring + size_t(NC) * (D * 4 + 8));
+            // CTA c's share of the merge rows: rows [lo, lo + rows), a team of
+            // `team` warps per row when there are fewer rows than warps, and
+            // this warp's first row descriptor
             const int64_t R = a.num_merge_rows;
-            const int64_t mlo = R * blockIdx.x / gridDim.x;
-            const int mrows = int(R * (blockIdx.x + 1) / gridDim.x - mlo);
-            const int team = (mrows >= NC || mrows == 0) ? 1 : NC / mrows;
-            const bool has = team == 1 ? warp < mrows : warp < mrows * team;
-            const int4 meta0 = has ? __ldg(a.merge_rows + mlo + (team == 1 ? warp : warp % mrows))
-                                   : make_int4(0, 0, 0, 0);
+            const auto share = [&](unsigned c, int64_t &lo, int &rows, int &team) {
+                lo = R * c / gridDim.x;
+                rows = int(R * (c + 1) / gridDim.x - lo);
+                team = (rows >= NC || rows == 0) ? 1 : NC / rows;
+                const bool has = team == 1 ? warp < rows : warp < rows * team;
+                return has ? __ldg(a.merge_rows + lo + (team == 1 ? warp : warp % rows)) : make_int4(0, 0, 0, 0);
+            };
+            int64_t mlo;
+            int mrows, team;
+            const int4 meta0 = share(blockIdx.x, mlo, mrows, team);   // loads while the CTAs gather
             named_barrier_sync(1, NC * 32);   // this CTA's partials are written
-            if (warp == 0 && lane == 0 && !grid_barrier(a.ticket, gridDim.x)) {
-                atomicOr(a.error, kErrTimeout);
-                flags->abort = 1;
+            unsigned nleft = 0;
+            if (warp == 0 && lane == 0) {
+                const int r = grid_arrive(a.gb, gridDim.x, blockIdx.x, &nleft);
+                if (r == kBarrierTimeout) {
+                    atomicOr(a.error, kErrTimeout);
+                    flags->abort = 1;
+                }
+                if (r == kBarrierGoMergeLeft)
+                    for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) left_snap[w] = __ldcg(a.gb.left + w);
+                flags->barrier = r;
             }
             named_barrier_sync(1, NC * 32);
+            const int verdict = flags->barrier;
             // After an abort a TMA load may still be landing in the ring: no merge.
-            if (!flags->abort)
+            if (!flags->abort && verdict != kBarrierLeft) {
                 merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
+                if (verdict == kBarrierGoMergeLeft) {
+                    // this CTA completed the barrier after others left: merge their shares too
+                    for (unsigned c = 0; c < gridDim.x; ++c) {
+                        if (c == blockIdx.x || !((left_snap[c / 64] >> (c % 64)) & 1ull)) continue;
+                        int64_t clo;
+                        int crows, cteam;
+                        const int4 cmeta0 = share(c, clo, crows, cteam);
+                        named_barrier_sync(1, NC * 32);   // the scratch is free again
+                        merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, clo, crows, cteam, cmeta0,
+                                                             xpar, xe);
+                    }
+                    named_barrier_sync(1, NC * 32);
+                    if (warp == 0 && lane == 0) {   // clear the leaves for the next launch
+                        for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) atomicAnd(a.gb.left + w, ~left_snap[w]);
+                        atomicAdd(a.gb.count, 0ull - (unsigned long long)nleft * kLeftUnit);
+                        atomicAdd(a.fallbacks, 1u);
+                    }
+                }
+            }
         }
         if (a.xworld) {
             // This CTA's rows are published (tagged) as they are written; merge

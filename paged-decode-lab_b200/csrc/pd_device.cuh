@@ -16,6 +16,9 @@ constexpr unsigned kFullMask = 0xffffffffu;
 // A barrier that has not completed after this long means the pipeline is
 // broken; the kernel records PD_DEVERR_TIMEOUT and unwinds instead of hanging.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
+// A CTA waiting at a plain launch's grid barrier leaves after this long if a
+// CTA of the launch has not started (grid_arrive).
+constexpr uint32_t kBarrierLeaveNs = 50000u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -97,24 +100,68 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     return v;
 }
 
-// Grid-wide barrier of a cooperative launch on a 64-bit ticket counter that
-// only ever grows: each of the `ctas` CTAs adds one per launch, so this
-// launch's barrier is complete once the counter reaches the next multiple of
-// `ctas` above this CTA's ticket (no reset between launches).  Called by one
-// thread per CTA after the CTA's own barrier; its writes before the call are
-// visible to every CTA after it.  False after the timeout.
-__device__ __forceinline__ bool grid_barrier(unsigned long long *ticket, unsigned ctas,
-                                             unsigned long long timeout_ns = kWaitTimeoutNs) {
+// Grid-wide barrier on counters that only ever grow (no reset between
+// launches, so CUDA-graph replays work).  `count` holds the arrivals in its
+// low 54 bits: each of the `ctas` CTAs adds one per launch, and this launch's
+// barrier is complete once they reach the next multiple of `ctas` above the
+// CTA's own ticket.  `started` gets one per CTA per launch as the CTA starts.
+//
+// Under a cooperative launch (leave_mode 0) every CTA is resident and a CTA
+// simply waits.  A plain launch does not promise that: an SM partition or a
+// kernel in another stream can hold back some CTAs until others exit.  So with
+// leave_mode 1 a CTA that has waited leave_ns while `started` shows a CTA of
+// this launch not yet started leaves instead: it sets its bit in `left` and
+// adds 2^54 to `count`.  The CTA whose arrival completes the barrier reads the
+// number that left in the high bits of its ticket and merges their shares as
+// well as its own; a CTA whose leave comes after that arrival takes it back
+// and stays.  leave_mode 2 leaves at the first wait (tests the path).
+enum : int { kBarrierGo = 0, kBarrierGoMergeLeft = 1, kBarrierLeft = 2, kBarrierTimeout = 3 };
+constexpr int kArrivalBits = 54;
+constexpr unsigned long long kArrivalMask = (1ull << kArrivalBits) - 1;
+constexpr unsigned long long kLeftUnit = 1ull << kArrivalBits;
+
+struct GridBarrier {
+    unsigned long long *count;     // arrivals (low 54 bits), CTAs that left (high 10 bits)
+    unsigned long long *started;   // CTAs started, over all launches
+    unsigned long long *left;      // one bit per CTA that left this launch's barrier (1024 bits)
+    uint32_t leave_mode;           // 0 wait, 1 leave after leave_ns if a CTA has not started, 2 leave at once
+    uint32_t leave_ns;
+};
+
+// Called by one thread per CTA after the CTA's own barrier; its writes before
+// the call are visible to every CTA that returns kBarrierGo*.  `*left_count`
+// gets the number of CTAs that left (kBarrierGoMergeLeft only).
+__device__ __forceinline__ int grid_arrive(const GridBarrier &gb, unsigned ctas, unsigned cta,
+                                           unsigned *left_count,
+                                           unsigned long long timeout_ns = kWaitTimeoutNs) {
     __threadfence();
-    const unsigned long long mine = atomicAdd(ticket, 1ull);
-    const unsigned long long target = (mine / ctas + 1) * ctas;
-    if (ld_acquire_u64(ticket) < target) {
-        const unsigned long long start = global_ns();
-        while (ld_acquire_u64(ticket) < target)
-            if (global_ns() - start > timeout_ns) return false;
+    const unsigned long long old = atomicAdd(gb.count, 1ull);
+    const unsigned long long target = ((old & kArrivalMask) / ctas + 1) * ctas;
+    if ((old & kArrivalMask) + 1 == target) {
+        __threadfence();
+        *left_count = unsigned(old >> kArrivalBits);
+        return *left_count ? kBarrierGoMergeLeft : kBarrierGo;
+    }
+    const unsigned long long start = global_ns();
+    for (;;) {
+        if ((ld_acquire_u64(gb.count) & kArrivalMask) >= target) break;
+        const unsigned long long t = global_ns() - start;
+        if (gb.leave_mode == 2 ||
+            (gb.leave_mode == 1 && t > gb.leave_ns && ld_acquire_u64(gb.started) < target)) {
+            const unsigned long long bit = 1ull << (cta & 63);
+            atomicOr(gb.left + cta / 64, bit);
+            __threadfence();
+            const unsigned long long o = atomicAdd(gb.count, kLeftUnit);
+            if ((o & kArrivalMask) < target) return kBarrierLeft;
+            // the barrier completed first: take the leave back and stay
+            atomicAdd(gb.count, 0ull - kLeftUnit);
+            atomicAnd(gb.left + cta / 64, ~bit);
+            break;
+        }
+        if (t > timeout_ns) return kBarrierTimeout;
     }
     __threadfence();
-    return true;
+    return kBarrierGo;
 }
 
 // Release at system scope: the caller's earlier writes (and those it has

@@ -227,7 +227,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
             }
     }
     p.sm_count = sm_count;
-    p.merge_in_kernel = !p.merge_rows.empty() && sm_count > 0 && C <= sm_count;
+    p.merge_in_kernel = !p.merge_rows.empty() && sm_count > 0 && C <= sm_count && C <= 1024;
     p.cta_off.assign(size_t(C) + 1, 0);
     p.segs.clear();
     for (int64_t i = 0; i < C; ++i) {
@@ -266,7 +266,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // ---------------------------------------------------------------- device image
     DeviceImage &im = p.image;
     size_t off = 0;
-    im.off_error = off;    off = align256(off + 16);
+    im.off_error = off;    off = align256(off + 192);
     im.off_head = off;     off = align256(off + p.head.size() * 4);
     im.off_segs = off;     off = align256(off + p.segs.size() * 4);
     im.off_groups = off;   off = align256(off + p.groups.size() * 4);

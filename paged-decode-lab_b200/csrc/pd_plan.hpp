@@ -18,7 +18,9 @@ pd_status fail(pd_status status, const std::string &msg);
 const std::string &last_error();
 
 struct DeviceImage {
-    // off_error: 16 bytes, the error word at +0 and the grid-barrier ticket (u64) at +8
+    // off_error: 256 bytes.  +0 the error word (u32), +4 the count of launches whose
+    // grid barrier fell back to merging for CTAs that left (u32), +8 the barrier's
+    // arrival count (u64), +16 its started count (u64), +64 its left-CTA bits (16 x u64)
     size_t off_error = 0, off_head = 0, off_segs = 0, off_groups = 0, off_merge = 0, off_lengths = 0;
     size_t off_table = 0, off_part_o = 0, off_part_ml = 0, bytes = 0;
 };
@@ -54,6 +56,9 @@ struct pd_plan {
     bool merge_in_kernel = false;  // split groups merged by the decode CTAs after a grid barrier
     bool dynamic = false;          // work covers max_lengths; live lengths / table read at launch
     int32_t max_span = 0;          // longest sequence the work list covers (max_lengths or lengths)
+    int32_t barrier_mode = 0;      // PD_BARRIER_*: how the grid barrier before the merge is launched
+    const void *occ_fn = nullptr;  // kernel whose co-resident CTA count is cached in occ_ctas
+    int32_t occ_ctas = 0;
     std::vector<int32_t> table;    // [B * W]
     std::vector<int32_t> lengths;  // [B]
     std::vector<int32_t> cta_off;  // [C + 1]

@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 PD_OK, PD_ERR_VALUE, PD_ERR_TYPE, PD_ERR_CUDA, PD_ERR_DEVICE, PD_ERR_UNBOUND = range(6)
 PD_FLOAT16, PD_FLOAT32 = 0, 1
 PD_DEVERR_TIMEOUT, PD_DEVERR_BAD_PAGE = 1, 2
+PD_BARRIER_PLAIN, PD_BARRIER_COOPERATIVE, PD_BARRIER_LEAVE_AT_ONCE = 0, 1, 2
 
 # Every function the header declares, with its ctypes signature.
 _c_int32, _c_int64, _c_size, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p
@@ -59,12 +60,15 @@ SIGNATURES = {
     "pd_merge_shards": (_c_int32, [_vp, _vp, _c_int32, _c_int64, _c_int64, _c_int32, _vp, _vp]),
     "pd_gather_debug": (_c_int32, [_vp, _vp, _vp, _c_int32, _vp, _vp, _vp]),
     "pd_plan_read_errors": (_c_int32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "pd_plan_set_barrier": (_c_int32, [_vp, _c_int32]),
+    "pd_plan_read_barrier_fallbacks": (_c_int32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "pd_decode_static": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
     "pd_static_scratch_capacity": (_c_size, []),
     "pd_status_string": (ctypes.c_char_p, [_c_int32]),
     "pd_last_error": (ctypes.c_char_p, []),
     "pd_abi_version": (_c_int32, []),
     "pd_selftest_wait_timeouts": (_c_int32, [_c_int32, ctypes.c_uint32, _vp]),
+    "pd_selftest_barrier_leave": (_c_int32, [_c_int32, ctypes.c_uint32, _vp]),
 }
 
 _lib = None
@@ -83,7 +87,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 4:
+        if lib.pd_abi_version() != 5:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

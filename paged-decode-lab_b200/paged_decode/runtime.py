@@ -179,6 +179,7 @@ class DecodePlan:
                         for code in (_native.PD_FLOAT16, _native.PD_FLOAT32)}
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
                                 dtype=torch.float32, device=self.device)
+        self.barrier = "plain"
 
     @classmethod
     def from_csr(cls, layout: Layout, indptr, indices, last_page_len, **kwargs):
@@ -317,6 +318,32 @@ class DecodePlan:
                                                 dtype, dense_k.data_ptr(), dense_v.data_ptr(), stream),
                       "gather")
         return dense_k, dense_v
+
+    def set_barrier(self, mode):
+        """How the grid barrier before the in-kernel merge is launched (extension;
+        see pd_plan_set_barrier): "plain" (default: a plain launch whose CTAs
+        leave the barrier when another CTA has not started, the last one then
+        merging for them), "cooperative" (all CTAs resident, or the merge
+        kernel), or "leave_at_once" (every waiting CTA leaves; tests the fallback)."""
+        codes = {"plain": _native.PD_BARRIER_PLAIN, "cooperative": _native.PD_BARRIER_COOPERATIVE,
+                 "leave_at_once": _native.PD_BARRIER_LEAVE_AT_ONCE}
+        if mode not in codes:
+            raise ValueError(f"barrier mode must be one of {sorted(codes)}")
+        for plan in self._native.values():
+            _native.check(self._lib.pd_plan_set_barrier(plan.handle, codes[mode]))
+        self.barrier = mode
+
+    def read_barrier_fallbacks(self):
+        """Return and clear the number of launches whose grid barrier fell back to
+        merging for CTAs that left (synchronises the current stream)."""
+        import torch
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        total = 0
+        for plan in self._native.values():
+            count = ctypes.c_uint32(0)
+            _native.check(self._lib.pd_plan_read_barrier_fallbacks(plan.handle, ctypes.byref(count), stream))
+            total += int(count.value)
+        return total
 
     def read_errors(self):
         """Return and clear the device error words (synchronises the current stream)."""

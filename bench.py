@@ -49,7 +49,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn µs/step + achieved HBM TB/s vs ~8 TB/s peak at 1/2/4/8 B200"
 L2_BYTES = 126 * 2**20
 DEFAULT_STEPS, DEFAULT_WARMUP = 200, 5
-GRAPH_STEPS = 10            # e2e steps per captured CUDA graph (one GPU)
+GRAPH_STEPS = 50            # default e2e steps per captured CUDA graph (one GPU; --graph-steps)
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode-kernel launch (the
 # 4th of `bench.py --workload W --steps 1 --warmup 3`), one ncu capture per
@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3a", "c3b", "c3c", "c4", "c5"])
+    ap.add_argument("--graph-steps", type=int, default=GRAPH_STEPS,
+                    help="e2e decode steps (with their copies) per captured CUDA graph on one GPU")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="N > 1: weak = KV-head shards of an N x larger model; strong = split this config")
     ap.add_argument("--sharding", choices=["kv_head", "sequence"], default=None,
@@ -278,11 +280,13 @@ class RankJob:
         self.bytes_total = algorithmic_bytes(w)
         self.extra_kernels = 0
         self.close = lambda: None
+        self.run_into = lambda q, out: out.copy_(self.run(q))   # sharded plans return their own output
         if world == 1:
             from paged_decode.runtime import DecodePlan
             self.plan = DecodePlan(L, w.table, w.lengths, split_tokens=w.split_tokens)
             self.q, self.k, self.v = w.tensors("cuda")
             self.run = lambda q: self.plan.run(q, self.k, self.v)
+            self.run_into = lambda q, out: self.plan.run(q, self.k, self.v, out=out)
             self.decode_plan = self.plan
             self.bytes_rank = self.bytes_total
             return
@@ -400,8 +404,9 @@ def run_ours(args, rank, local, world):
     # (2) e2e through the public API with host buffers.  Every step copies its q
     # from pinned host memory and its FP32 output back; the two directions run
     # on their own streams, double-buffered, so step i+1's input and step i-1's
-    # output move while step i decodes.  On
-    # one GPU, GRAPH_STEPS such steps (their copies included) are captured once
+    # output move while step i decodes (on one GPU the decode writes straight
+    # into the staging buffer the output is copied back from).  On
+    # one GPU, --graph-steps such steps (their copies included) are captured once
     # through the same public calls and replayed, so the host's per-call
     # overhead does not set the pace.
     e2e = None
@@ -428,7 +433,7 @@ def run_ours(args, rank, local, world):
             main.wait_event(h2d_done[b])
             if not fresh:
                 main.wait_event(d2h_done[b])          # stage[b] drained by step i-2's copy
-            stage[b].copy_(job.run(q_dev[b]))
+            job.run_into(q_dev[b], stage[b])
             computed[b].record(main)
             with torch.cuda.stream(copy):
                 copy.wait_event(computed[b])
@@ -446,16 +451,16 @@ def run_ours(args, rank, local, world):
             with torch.cuda.graph(graph, stream=cap):
                 copy.wait_stream(cap)
                 upload.wait_stream(cap)
-                for i in range(GRAPH_STEPS):
+                for i in range(args.graph_steps):
                     if flush is not None:
                         flush.amax()
                     e2e_step(i, cap, fresh=i < 2)
                 cap.wait_stream(copy)
                 cap.wait_stream(upload)
-            reps = -(-args.steps // GRAPH_STEPS)
+            reps = -(-args.steps // args.graph_steps)
             graph.replay()
             torch.cuda.synchronize()
-        timed = reps * GRAPH_STEPS if graph is not None else args.steps
+        timed = reps * args.graph_steps if graph is not None else args.steps
         barrier(world)
         t0 = time.perf_counter()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -490,9 +495,11 @@ def run_ours(args, rank, local, world):
                "d2h_bytes_per_step": out_host[0].numel() * 4,
                "wall_s": time.perf_counter() - t0,
                "steps": timed,
-               "path": ("public API run() (ctypes -> C ABI pd_decode); pinned host q in and FP32 out back "
+               "path": ("public API run() (ctypes -> C ABI pd_decode"
+                        + (", out= the staging buffer" if world == 1 else "")
+                        + "); pinned host q in and FP32 out back "
                         "every step, each direction on its own stream, double-buffered"
-                        + (f"; {GRAPH_STEPS} steps captured once as a CUDA graph and replayed"
+                        + (f"; {args.graph_steps} steps captured once as a CUDA graph and replayed"
                            if world == 1 else ""))}
 
     peak, peak_kind = measured_peak()

@@ -231,14 +231,21 @@ class DecodePlan:
                 raise ValueError("inference only: detach tensors requiring gradients")
         return _native.PD_FLOAT16 if q.dtype == torch.float16 else _native.PD_FLOAT32
 
-    def run(self, q, k, v):
-        """Decode one step; returns the plan's borrowed FP32 [B, Hq, D] output."""
+    def run(self, q, k, v, out=None):
+        """Decode one step; returns the plan's borrowed FP32 [B, Hq, D] output, or
+        writes into ``out`` (extension: a contiguous FP32 [B, Hq, D] tensor on the
+        plan device) and returns it."""
         import torch
         dtype = self._check_inputs(q, k, v)
+        if out is None:
+            out = self._out
+        elif (tuple(out.shape) != tuple(self._out.shape) or out.dtype != torch.float32 or
+              out.device != self.device or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous FP32 [B,Hq,D] tensor on the plan device")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _native.check(self._lib.pd_decode(self._native[dtype].handle, q.data_ptr(), k.data_ptr(),
-                                          v.data_ptr(), dtype, self._out.data_ptr(), stream), "decode")
-        return self._out
+                                          v.data_ptr(), dtype, out.data_ptr(), stream), "decode")
+        return out
 
     def run_with_stats(self, q, k, v, out, stats):
         """Decode into caller buffers: out FP32 [B,Hq,D] and stats FP32 [B,Hq,2] = (m, l).

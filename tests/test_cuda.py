@@ -445,3 +445,19 @@ def test_maximum_batch_of_65535_sequences():
     out = plan.run(q, k, v).cpu().numpy()
     np.testing.assert_allclose(out, _c_oracle(q, k, v, table, lengths), atol=2e-3, rtol=1e-3)
     assert not out[lengths == 0].any() and plan.read_errors() == 0
+
+
+def test_run_into_a_caller_buffer():
+    """run(..., out=buf) writes the same bits into the caller's buffer and returns it."""
+    layout, table, lengths = _fragmented(3, 16, 4, 128, 16, [7, 900, 2500], seed=12)
+    q, k, v = make_tensors(layout, seed=12)
+    plan = DecodePlan(layout, table, lengths)
+    ref = plan.run(q, k, v).clone()
+    buf = torch.full_like(ref, float("nan"))
+    assert plan.run(q, k, v, out=buf) is buf
+    assert torch.equal(buf, ref)
+    for bad in (torch.empty_like(ref, dtype=torch.float16), ref[:, :, :64], ref.cpu(),
+                torch.empty((3, 16, 256), device=ref.device)[:, :, :128]):
+        with pytest.raises(ValueError):
+            plan.run(q, k, v, out=bad)
+    assert plan.read_errors() == 0

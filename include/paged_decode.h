@@ -77,8 +77,9 @@ typedef struct pd_plan_info {
     int32_t heads_per_tile;  /* KV heads gathered per page tile (1, 2, 4 or 8) */
     int32_t total_pages;     /* page tiles streamed per decode (all groups) */
     int32_t merge_rows;      /* output rows merged from partials after the decode */
-    int32_t merge_in_kernel; /* 1: the decode CTAs merge them after a grid barrier (cooperative
-                                launch; num_ctas <= SMs), 0: a dependent merge kernel does */
+    int32_t merge_in_kernel; /* 1: the decode CTAs merge them after a grid barrier
+                                (num_ctas <= SMs; see pd_plan_set_barrier), 0: a dependent
+                                merge kernel does */
     int32_t dynamic;         /* 1: built by pd_plan_create_dynamic */
     int32_t max_span;        /* longest sequence the work list covers (max_lengths, else lengths) */
     int64_t workspace_bytes; /* split-K partials + merge counters */
@@ -142,10 +143,11 @@ pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *s
 /* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
  * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
  * k and v must be 16-byte aligned (TMA); dtype must be the plan's.
- * Asynchronous on `stream`: one decode kernel (a cooperative launch that
- * also merges the partials when the plan has some and num_ctas <= SMs), or
- * the decode kernel and a dependent merge kernel.  Launches of one plan must
- * stay in one stream order: they share the plan's partial slots and barrier.
+ * Asynchronous on `stream`: one decode kernel (which also merges the
+ * partials after a grid barrier when the plan has some and num_ctas <= SMs;
+ * see pd_plan_set_barrier), or the decode kernel and a dependent merge
+ * kernel.  Launches of one plan must stay in one stream order: they share the
+ * plan's partial slots and barrier counters.
  */
 pd_status pd_decode(pd_plan *plan, const void *q, const void *k, const void *v, pd_dtype dtype,
                     float *out, void *stream);

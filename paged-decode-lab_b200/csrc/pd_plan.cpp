@@ -211,7 +211,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     p.num_pieces = int32_t(slots);
     // Output rows of the split groups, merged after the decode.  With no more
     // CTAs than SMs the decode CTAs can all be resident at once (one CTA per
-    // SM by construction), so a cooperative launch can merge them in-kernel.
+    // SM by construction), so they merge them in-kernel after a grid barrier.
     // Each row: {output row b * Hq + query head, first slot, segments, column
     // hh * GT + q of the [slot][HG][GT] partial layout}.
     p.merge_rows.clear();

@@ -218,9 +218,9 @@ def _sm_count():
     (torch.float16, 128, 32, 8, 16), (torch.float16, 64, 16, 2, 32), (torch.float32, 64, 8, 8, 16),
     (torch.float32, 128, 16, 4, 32), (torch.float16, 128, 32, 1, 32)])
 def test_in_kernel_merge_and_merge_kernel_agree(dtype, dim, heads, kv_heads, page):
-    """num_ctas <= SMs merges the partials inside the decode kernel (one cooperative
-    launch); more CTAs than SMs use the dependent merge kernel.  Both match the
-    oracle, and their (m, l) statistics agree."""
+    """num_ctas <= SMs merges the partials inside the decode kernel (one launch);
+    more CTAs than SMs use the dependent merge kernel.  Both match the oracle,
+    and their (m, l) statistics agree."""
     layout, table, lengths = _fragmented(3, heads, kv_heads, dim, page, [5, 3000, 6000], seed=dim + heads)
     q, k, v = make_tensors(layout, dtype=dtype, seed=4)
     expected = oracle(q, k, v, table, lengths)

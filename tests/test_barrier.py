@@ -140,3 +140,31 @@ def test_barrier_leaves_only_when_a_cta_has_not_started():
     assert lib.pd_selftest_barrier_leave(torch.cuda.current_device(), 200, outcomes) == 0
     assert list(outcomes) == [2, 1, 1, 3]
     assert time.time() - start < 10
+
+
+def test_two_plans_on_two_streams_share_the_gpu():
+    """Two one-kernel plans launched on two streams at once compete for SMs, so
+    neither grid can count on being resident (a CTA waiting for one of its own
+    launch that has not started would leave).  However the hardware interleaves
+    them, every launch of both gives the bits each gives alone."""
+    la, ta, na = _case(4, 32, 8, 128, 16, [3000, 500, 8000, 1200], 11)
+    lb, tb, nb = _case(3, 32, 8, 128, 16, [6000, 40, 2500], 12)
+    qa, ka, va = make_tensors(la, dtype=torch.float16, seed=11)
+    qb, kb, vb = make_tensors(lb, dtype=torch.float16, seed=12)
+    pa, pb = DecodePlan(la, ta, na), DecodePlan(lb, tb, nb)
+    assert pa.native_info(torch.float16).merge_in_kernel == 1 and pb.native_info(torch.float16).merge_in_kernel == 1
+    ref_a, ref_b = pa.run(qa, ka, va).clone(), pb.run(qb, kb, vb).clone()
+    sa, sb = torch.cuda.Stream(), torch.cuda.Stream()
+    outs_a = [torch.empty_like(ref_a) for _ in range(30)]
+    outs_b = [torch.empty_like(ref_b) for _ in range(30)]
+    torch.cuda.synchronize()
+    for i in range(30):
+        with torch.cuda.stream(sa):
+            pa.run(qa, ka, va, out=outs_a[i])
+        with torch.cuda.stream(sb):
+            pb.run(qb, kb, vb, out=outs_b[i])
+    torch.cuda.synchronize()
+    for i in range(30):
+        assert torch.equal(outs_a[i], ref_a) and torch.equal(outs_b[i], ref_b), i
+    assert pa.read_errors() == 0 and pb.read_errors() == 0
+    print("barrier fallbacks under contention:", pa.read_barrier_fallbacks(), pb.read_barrier_fallbacks())

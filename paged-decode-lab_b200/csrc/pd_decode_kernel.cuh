@@ -600,6 +600,76 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
                                                 unsigned xe) {
     using M = RowMerge<D, HG, GT, NSUB>;
     M rm;
+    if constexpr (NC <= 4 && M::LP == 1) {
+        if (team == 1) {
+            // Four or fewer consumer warps: each merges many rows (config 3c: ~7
+            // of ~3 partials each).  The partials of a warp's rows form one
+            // stream, U loads in flight across row boundaries, so the warp
+            // waits for one L2 round trip per U partials, not one per row.
+            // Each row still adds its partials in slot order, as fold() does.
+            const int K = rows > warp ? (rows - warp + NC - 1) / NC : 0;
+            for (int k0 = 0; k0 < K; k0 += 32) {
+                const int kn = min(32, K - k0);
+                // lane i: descriptor of row k0 + i (merge rows have >= 1 segment)
+                const int4 mine = (k0 == 0 && lane == 0) ? meta0
+                                  : lane < kn ? __ldg(a.merge_rows + lo + warp + int64_t(k0 + lane) * NC)
+                                              : make_int4(0, 0, 0, 0);
+                int k = 0, p = 0, cur = 0;
+                int4 mk = shfl_int4(mine, 0);
+                int pk = mk.z * NSUB;
+                rm.m = -INFINITY;
+                rm.l = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < M::CPL; ++cc) rm.o[cc] = make_float4(0.f, 0.f, 0.f, 0.f);
+                while (k < kn) {
+                    float2 ml[M::U];
+                    float4 ov[M::U][M::CPL];
+                    int rowof[M::U];
+#pragma unroll
+                    for (int u = 0; u < M::U; ++u) {
+                        rowof[u] = -1;
+                        if (k < kn) {
+                            const int64_t slot = int64_t(mk.y) + int64_t(p / NSUB) * a.slot_stride + p % NSUB;
+                            const int64_t pr = slot * (HG * GT) + mk.w;
+                            ml[u] = __ldcg(a.part_ml + pr);
+                            const float4 *src = reinterpret_cast<const float4 *>(a.part_o + pr * D);
+#pragma unroll
+                            for (int cc = 0; cc < M::CPL; ++cc) ov[u][cc] = __ldcg(src + lane + cc * 32);
+                            rowof[u] = k;
+                            if (++p == pk) {
+                                p = 0;
+                                if (++k < kn) {
+                                    mk = shfl_int4(mine, k);
+                                    pk = mk.z * NSUB;
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < M::U; ++u) {
+                        if (rowof[u] < 0) break;
+                        if (rowof[u] != cur) {   // row `cur` is complete
+                            const int4 mc = shfl_int4(mine, cur);
+                            rm.write(a, mc, lane, xpar);
+                            if (a.xworld) publish_rows<D>(a, mc.x, 1, xpar, xe, lane);
+                            rm.m = -INFINITY;
+                            rm.l = 0.f;
+#pragma unroll
+                            for (int cc = 0; cc < M::CPL; ++cc) rm.o[cc] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            cur = rowof[u];
+                        }
+                        rm.add(ml[u].x, ml[u].y, ov[u]);
+                    }
+                }
+                if (kn > 0) {
+                    const int4 mc = shfl_int4(mine, cur);
+                    rm.write(a, mc, lane, xpar);
+                    if (a.xworld) publish_rows<D>(a, mc.x, 1, xpar, xe, lane);
+                }
+            }
+            return;
+        }
+    }
     if (team == 1) {
         int4 meta = meta0;
         for (int r = warp; r < rows; r += NC) {

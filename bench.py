@@ -56,7 +56,7 @@ GRAPH_STEPS = 50            # default e2e steps per captured CUDA graph (one GPU
 # workload; config 4 (4.8 GB resident) was not captured.
 NCU_TRAFFIC_BYTES = {"c1": 67_258_880 + 571_648, "c2": 469_731_072 + 5_400_320,
                      "c3a": 2_150_068_480 + 7_169_792, "c3b": 67_789_056 + 1_476_096,
-                     "c3c": 540_691_712 + 4_820_736, "c5": 1_073_953_792 + 3_577_344}
+                     "c3c": 540_718_336 + 4_886_528, "c5": 1_073_953_792 + 3_577_344}
 
 
 def parse_args():

@@ -26,8 +26,9 @@ MODULE = "ref_paged_decode"
 SO_PATH = REF_DIR / f"{MODULE}.so"
 
 
-def build(reference_root="/root/reference", force=False):
-    """Compile the reference kernel; returns the .so path, or None if sources are absent."""
+def build(reference_root, force=False):
+    """Compile the reference kernel from the checkout at ``reference_root``; returns
+    the .so path, or None if its sources are absent (a prebuilt .so is kept)."""
     csrc = Path(reference_root) / "src" / "paged_decode" / "csrc"
     sources = [csrc / "bindings.cpp", csrc / "decode.cu"]
     if not all(s.exists() for s in sources):

@@ -138,3 +138,27 @@ def test_exchange_buffer_size():
         assert lib.pd_exchange_bytes(handle, 9) == 0 and lib.pd_exchange_bytes(None, 2) == 0
     finally:
         lib.pd_plan_destroy(handle)
+
+
+def test_barrier_mode_and_counters_on_a_host_only_plan():
+    """pd_plan_set_barrier accepts the three modes and nothing else; the counter
+    reads and the barrier self-test reject what they cannot use without touching
+    a GPU."""
+    lib = _native.load()
+    status, handle = _create((2, 8, 2, 128, 16, 4), [[0, 1], [2, 3]], [17, 32])
+    assert status == _native.PD_OK
+    try:
+        for mode in (_native.PD_BARRIER_PLAIN, _native.PD_BARRIER_COOPERATIVE, _native.PD_BARRIER_LEAVE_AT_ONCE):
+            assert lib.pd_plan_set_barrier(handle, mode) == _native.PD_OK
+        for bad in (-1, 3, 99):
+            assert lib.pd_plan_set_barrier(handle, bad) == _native.PD_ERR_VALUE
+        count = ctypes.c_uint32(7)
+        assert lib.pd_plan_read_barrier_fallbacks(handle, ctypes.byref(count), None) != _native.PD_OK
+        assert count.value == 7                               # untouched on error
+    finally:
+        lib.pd_plan_destroy(handle)
+    assert lib.pd_plan_set_barrier(None, 0) == _native.PD_ERR_VALUE
+    outcomes = (ctypes.c_uint32 * 4)()
+    assert lib.pd_selftest_barrier_leave(0, 0, outcomes) == _native.PD_ERR_VALUE        # leave_us 0
+    assert lib.pd_selftest_barrier_leave(0, 200000, outcomes) == _native.PD_ERR_VALUE   # above 1e5
+    assert lib.pd_selftest_barrier_leave(0, 200, None) == _native.PD_ERR_VALUE

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 5
+#define PD_ABI_VERSION 6
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -82,7 +82,7 @@ typedef struct pd_plan_info {
                                 merge kernel does */
     int32_t dynamic;         /* 1: built by pd_plan_create_dynamic */
     int32_t max_span;        /* longest sequence the work list covers (max_lengths, else lengths) */
-    int64_t workspace_bytes; /* split-K partials + merge counters */
+    int64_t workspace_bytes; /* split-K partials, o and (m, l) (pd_plan_workspace_bytes) */
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
 } pd_plan_info;
 
@@ -139,6 +139,23 @@ size_t pd_plan_device_bytes(const pd_plan *plan);
  * to move the plan to a new buffer or to clear its error word and counters.
  */
 pd_status pd_plan_bind(pd_plan *plan, void *device_buffer, size_t bytes, void *stream);
+
+/* The two parts of pd_plan_device_bytes(): the plan's metadata (page table,
+ * work list, error word and barrier counters; uploaded by the bind) and its
+ * split-K workspace (partial outputs, written and read within each launch).
+ * Replace DecodePlan.workspace_bytes (runtime.py:71-73), which counts the
+ * reference's numerator and stats tensors. */
+size_t pd_plan_metadata_bytes(const pd_plan *plan);
+size_t pd_plan_workspace_bytes(const pd_plan *plan);
+
+/* As pd_plan_bind, with the metadata and the workspace in separate buffers
+ * (each >= its size above, 256-byte aligned; the workspace may be NULL when
+ * its size is 0).  A workspace carries nothing from one launch to the next,
+ * so plans whose launches stay in one stream order may share one (the Python
+ * DecodePlan binds its FP16 and FP32 plans to one workspace of the larger
+ * size).  No reference counterpart. */
+pd_status pd_plan_bind_split(pd_plan *plan, void *metadata, size_t metadata_bytes, void *workspace,
+                             size_t workspace_bytes, void *stream);
 
 /* One decode step.  Replaces ext.decode / decode_cuda (bindings.cpp:9,
  * decode.cu:197-246).  out receives FP32 [batch, query_heads, head_dim].
@@ -203,20 +220,29 @@ pd_status pd_gather_debug(pd_plan *plan, const void *k, const void *v, pd_dtype 
  * pd_plan_bind; its metadata and split-K partials go to one file-scope
  * device array of pd_static_scratch_capacity() bytes (16 MiB) that every
  * GPU loading this library holds until exit.  A plan needing more
- * (pd_plan_device_bytes) is rejected with PD_ERR_VALUE.  Each call uploads
- * the plan's metadata into the array on `stream` (overwriting the previous
- * call's contents and zeroing its error word), then launches.  All calls
- * share the array: calls that overlap on the GPU (other streams, devices'
- * own arrays aside) race.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress, with that device current); make that
- * first call before any stream capture.  Allocates nothing: no cudaMalloc,
- * cudaFree or allocating library routine.
+ * (pd_plan_device_bytes) is rejected with PD_ERR_VALUE, and so is a dynamic
+ * plan (its live metadata goes through pd_decode_dynamic).  Each call
+ * uploads the plan's metadata from host memory into the array on `stream`
+ * (overwriting the previous call's contents and zeroing its error word),
+ * then launches.  All calls share the array: calls that overlap on the GPU
+ * (other streams; each device has its own array) race.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current) and keeps it for the life of the process; make that
+ * first call before any stream capture, and none after a cudaDeviceReset.
+ * Read the kernel's error word with pd_static_read_errors.  Allocates
+ * nothing: no cudaMalloc, cudaFree or allocating library routine.
  */
 pd_status pd_decode_static(pd_plan *plan, const void *q, const void *k, const void *v,
                            pd_dtype dtype, float *out, void *stream);
 
 /* Size of the device array pd_decode_static uses (bytes). */
 size_t pd_static_scratch_capacity(void);
+
+/* The error word (PD_DEVERR_* bits) that the last pd_decode_static call on
+ * `device` left in the array: copied to *error_word and cleared
+ * (synchronises `stream`).  No counterpart in the reference; allocates
+ * nothing. */
+pd_status pd_static_read_errors(int32_t device, uint32_t *error_word, void *stream);
 
 /* Copy the device error word to *error_word and clear it (synchronises `stream`). */
 pd_status pd_plan_read_errors(pd_plan *plan, uint32_t *error_word, void *stream);

@@ -125,8 +125,11 @@ DecodeArgs make_args_at(pd_plan *p, uint8_t *dev, const void *q, float *out, flo
     a.head = reinterpret_cast<const int4 *>(dev + im.off_head);
     a.segs = reinterpret_cast<const int4 *>(dev + im.off_segs);
     a.groups = reinterpret_cast<const int4 *>(dev + im.off_groups);
-    a.part_o = reinterpret_cast<float *>(dev + im.off_part_o);
-    a.part_ml = reinterpret_cast<float2 *>(dev + im.off_part_ml);
+    // the split-K partials: in the plan's own buffer, or in a workspace bound
+    // apart from the metadata (pd_plan_bind_split, shareable between plans)
+    uint8_t *ws = (p->ws && dev == p->dev) ? p->ws : dev + im.off_part_o;
+    a.part_o = reinterpret_cast<float *>(ws);
+    a.part_ml = reinterpret_cast<float2 *>(ws + (im.off_part_ml - im.off_part_o));
     a.out = out;
     a.stats = stats;
     a.error = reinterpret_cast<uint32_t *>(dev + im.off_error);
@@ -352,11 +355,13 @@ PD_API pd_status pd_plan_copy_worklist(const pd_plan *p, int32_t *segments, int3
 
 PD_API size_t pd_plan_device_bytes(const pd_plan *p) { return p ? p->image.bytes : 0; }
 
-PD_API pd_status pd_plan_bind(pd_plan *p, void *buffer, size_t bytes, void *stream) {
+namespace {
+// Upload the plan's metadata into `buffer` (>= `need` bytes) and bind it.
+pd_status bind_impl(pd_plan *p, void *buffer, size_t bytes, size_t need, void *stream) {
     if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
     if (p->device < 0) return fail(PD_ERR_VALUE, "host-only plan (device < 0) cannot be bound");
-    if (!buffer || bytes < p->image.bytes)
-        return fail(PD_ERR_VALUE, "device buffer is NULL or smaller than pd_plan_device_bytes()");
+    if (!buffer || bytes < need)
+        return fail(PD_ERR_VALUE, "device buffer is NULL or smaller than the plan needs");
     if (reinterpret_cast<uintptr_t>(buffer) & 255)
         return fail(PD_ERR_VALUE, "device buffer must be 256-byte aligned");
     DeviceGuard guard(p->device);
@@ -370,6 +375,32 @@ PD_API pd_status pd_plan_bind(pd_plan *p, void *buffer, size_t bytes, void *stre
         return fail(PD_ERR_CUDA, std::string("plan upload: ") + cudaGetErrorString(err));
     p->dev = static_cast<uint8_t *>(buffer);
     p->dev_bytes = bytes;
+    p->ws = nullptr;
+    return PD_OK;
+}
+}  // namespace
+
+PD_API pd_status pd_plan_bind(pd_plan *p, void *buffer, size_t bytes, void *stream) {
+    return bind_impl(p, buffer, bytes, p ? p->image.bytes : 0, stream);
+}
+
+PD_API size_t pd_plan_metadata_bytes(const pd_plan *p) { return p ? p->image.off_part_o : 0; }
+
+PD_API size_t pd_plan_workspace_bytes(const pd_plan *p) {
+    return p ? p->image.bytes - p->image.off_part_o : 0;
+}
+
+PD_API pd_status pd_plan_bind_split(pd_plan *p, void *metadata, size_t metadata_bytes, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+    if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
+    const size_t ws_need = p->image.bytes - p->image.off_part_o;
+    if (ws_need > 0 && (!workspace || workspace_bytes < ws_need))
+        return fail(PD_ERR_VALUE, "workspace is NULL or smaller than pd_plan_workspace_bytes()");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(PD_ERR_VALUE, "workspace must be 256-byte aligned");
+    const pd_status s = bind_impl(p, metadata, metadata_bytes, p->image.off_part_o, stream);
+    if (s != PD_OK) return s;
+    p->ws = ws_need > 0 ? static_cast<uint8_t *>(workspace) : nullptr;
     return PD_OK;
 }
 
@@ -456,6 +487,10 @@ PD_API pd_status pd_decode_static(pd_plan *p, const void *q, const void *k, cons
                                   float *out, void *stream) {
     if (!p) return fail(PD_ERR_VALUE, "plan must not be NULL");
     if (p->device < 0) return fail(PD_ERR_VALUE, "host-only plan (device < 0) cannot launch");
+    // A dynamic plan decodes live metadata that only pd_decode_dynamic takes.
+    if (p->dynamic)
+        return fail(PD_ERR_VALUE, "pd_decode_static takes plans from pd_plan_create; "
+                                  "a dynamic plan needs pd_decode_dynamic");
     pd_status s = check_dtype(p, dtype);
     if (s != PD_OK) return s;
     if (!q || !out) return fail(PD_ERR_VALUE, "q and out must not be NULL");
@@ -480,6 +515,27 @@ PD_API pd_status pd_decode_static(pd_plan *p, const void *q, const void *k, cons
         return fail(PD_ERR_CUDA, std::string("scratch upload: ") + cudaGetErrorString(err));
     const DecodeArgs args = make_args_at(p, scratch, q, out, nullptr);
     return launch(p, k, v, dtype, kModeDecode, args, stream);
+}
+
+PD_API pd_status pd_static_read_errors(int32_t device, uint32_t *error_word, void *stream) {
+    if (!error_word) return fail(PD_ERR_VALUE, "error_word must not be NULL");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    uint8_t *scratch = nullptr;
+    pd_status s = static_scratch(device, &scratch);
+    if (s != PD_OK) return s;
+    // Every plan image starts with its error word (offset 0), so the last
+    // static call's word sits at the start of the array.
+    auto st = static_cast<cudaStream_t>(stream);
+    uint32_t word = 0;
+    cudaError_t err = cudaMemcpyAsync(&word, scratch, 4, cudaMemcpyDeviceToHost, st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(scratch, 0, 4, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("static error word read: ") + cudaGetErrorString(err));
+    *error_word = word;
+    return PD_OK;
 }
 
 PD_API pd_status pd_gather_debug(pd_plan *p, const void *k, const void *v, pd_dtype dtype,

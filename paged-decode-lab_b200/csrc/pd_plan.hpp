@@ -18,7 +18,7 @@ pd_status fail(pd_status status, const std::string &msg);
 const std::string &last_error();
 
 struct DeviceImage {
-    // off_error: 256 bytes.  +0 the error word (u32), +4 the count of launches whose
+    // off_error is always 0 (pd_static_read_errors relies on it).  256 bytes:  +0 the error word (u32), +4 the count of launches whose
     // grid barrier fell back to merging for CTAs that left (u32), +8 the barrier's
     // arrival count (u64), +16 its started count (u64), +64 its left-CTA bits (16 x u64)
     size_t off_error = 0, off_head = 0, off_segs = 0, off_groups = 0, off_merge = 0, off_lengths = 0;
@@ -70,6 +70,7 @@ struct pd_plan {
     std::vector<uint8_t> host_image;  // metadata part of the device buffer
     uint8_t *dev = nullptr;           // bound device buffer (caller-owned)
     size_t dev_bytes = 0;
+    uint8_t *ws = nullptr;            // split-K workspace bound apart from `dev` (pd_plan_bind_split)
     pd::TensorMapCache tmaps;
 };
 

@@ -48,6 +48,9 @@ SIGNATURES = {
     "pd_plan_copy_worklist": (_c_int32, [_vp, _vp, _vp, _vp]),
     "pd_plan_device_bytes": (_c_size, [_vp]),
     "pd_plan_bind": (_c_int32, [_vp, _vp, _c_size, _vp]),
+    "pd_plan_metadata_bytes": (_c_size, [_vp]),
+    "pd_plan_workspace_bytes": (_c_size, [_vp]),
+    "pd_plan_bind_split": (_c_int32, [_vp, _vp, _c_size, _vp, _c_size, _vp]),
     "pd_decode": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
     "pd_decode_dynamic": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp, _vp, _vp, _vp]),
     "pd_exchange_bytes": (_c_size, [_vp, _c_int32]),
@@ -64,6 +67,7 @@ SIGNATURES = {
     "pd_plan_read_barrier_fallbacks": (_c_int32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "pd_decode_static": (_c_int32, [_vp, _vp, _vp, _vp, _c_int32, _vp, _vp]),
     "pd_static_scratch_capacity": (_c_size, []),
+    "pd_static_read_errors": (_c_int32, [_c_int32, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "pd_status_string": (ctypes.c_char_p, [_c_int32]),
     "pd_last_error": (ctypes.c_char_p, []),
     "pd_abi_version": (_c_int32, []),
@@ -87,7 +91,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 5:
+        if lib.pd_abi_version() != 6:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

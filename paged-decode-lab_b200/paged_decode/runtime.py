@@ -102,21 +102,21 @@ def inspect_plan(layout: Layout, table, lengths, *, split_tokens=256, num_ctas=1
             "segments": segs, "groups": groups, "cta_offsets": offsets}
 
 
+def _align256(n):
+    return (int(n) + 255) // 256 * 256
+
+
 class _NativePlan:
-    """One C-ABI plan (one input dtype) and the device buffer it is bound to."""
+    """One C-ABI plan (one input dtype); ``DecodePlan`` binds it to device memory."""
 
     def __init__(self, lib, layout, table, lengths, split_tokens, merge, dtype_code, device, num_ctas,
                  max_lengths=None):
-        import torch
         self._lib = lib
         self.handle = _native_plan(layout, table, lengths, split_tokens, merge, dtype_code,
                                    device.index, num_ctas, max_lengths)
         self.info, self.segments, self.groups, self.cta_offsets = _worklist(lib, self.handle)
-        nbytes = int(lib.pd_plan_device_bytes(self.handle))
-        self.buffer = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
-        stream = torch.cuda.current_stream(device).cuda_stream
-        _native.check(lib.pd_plan_bind(self.handle, self.buffer.data_ptr(), self.buffer.numel(), stream),
-                      "bind")
+        self.metadata_bytes = int(lib.pd_plan_metadata_bytes(self.handle))
+        self.workspace_bytes = int(lib.pd_plan_workspace_bytes(self.handle))
 
     def __del__(self):
         handle = getattr(self, "handle", None)
@@ -126,19 +126,27 @@ class _NativePlan:
 
 
 class DecodePlan:
-    """Static metadata + reusable workspace for one decode shape.
+    """A decode plan for one batch's fixed metadata, reusable across steps.
 
-    table/lengths are CPU integer arrays and are copied during construction.
-    KV contents and q can change between runs; metadata requires a new plan.
-    The output is borrowed storage, overwritten by the next run.  A plan may
-    be used on one stream at a time; use distinct plans for concurrent streams.
+    The constructor validates the layout and the CPU page table / lengths,
+    keeps its own copies of them, and lays out everything a decode step needs
+    on the device: a balanced work list and one split-K workspace.  Between
+    runs only the contents of q, k and v may change; new lengths or pages
+    need a new plan (or a dynamic plan, ``max_lengths``).  ``run`` hands back
+    the plan's own FP32 output tensor, which the next run overwrites.  Launch
+    a plan from one stream at a time; concurrent streams need a plan each.
 
-    ``merge`` is accepted for compatibility: the B200 path always merges split
-    partials the same way (a merge kernel launched programmatically dependent
-    on the decode kernel), and ``merge_implementation`` keeps the reference's
-    classification ("serial", "shared" or "serial_fallback", runtime.py:54).
-    ``num_ctas`` (extension) overrides the persistent grid size, which by
-    default is one CTA per SM.
+    ``merge`` is accepted for compatibility: the B200 path always merges
+    split partials the same way (inside the decode kernel after a grid
+    barrier, or in a dependent merge kernel), and ``merge_implementation``
+    keeps the reference's classification ("serial", "shared" or
+    "serial_fallback", runtime.py:54).  ``num_ctas`` (extension) overrides
+    the persistent grid size, which by default is one CTA per SM.
+
+    Each input dtype has its own native plan (page tiles are sized per
+    dtype).  Both live in one device buffer: their metadata side by side and
+    one shared split-K workspace of the larger size, since a plan's launches
+    stay in one stream order and a workspace carries nothing between them.
     """
 
     def __init__(self, layout: Layout, table, lengths, *, device="cuda", split_tokens=256,
@@ -173,10 +181,21 @@ class DecodePlan:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self._table_cpu, self._lengths_cpu = table, lengths
         self._lib = _native.load()
-        # one native plan per input dtype (page tiles are sized per dtype)
+        # one native plan per input dtype (page tiles are sized per dtype), in one
+        # buffer: [FP16 metadata][FP32 metadata][shared split-K workspace]
         self._native = {code: _NativePlan(self._lib, layout, table, lengths, split_tokens, merge, code,
                                           self.device, num_ctas, max_lengths)
                         for code in (_native.PD_FLOAT16, _native.PD_FLOAT32)}
+        metas = [_align256(n.metadata_bytes) for n in self._native.values()]
+        ws = _align256(max(n.workspace_bytes for n in self._native.values()))
+        self._buffer = torch.empty(max(sum(metas) + ws, 256), dtype=torch.uint8, device=self.device)
+        base = self._buffer.data_ptr()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        offset = 0
+        for plan, meta in zip(self._native.values(), metas):
+            _native.check(self._lib.pd_plan_bind_split(plan.handle, base + offset, meta,
+                                                       base + sum(metas) if ws else None, ws, stream), "bind")
+            offset += meta
         self._out = torch.empty((layout.batch, layout.query_heads, layout.head_dim),
                                 dtype=torch.float32, device=self.device)
         self.barrier = "plain"
@@ -200,8 +219,15 @@ class DecodePlan:
 
     @property
     def workspace_bytes(self):
-        """Split-K partial outputs and their (m, l) pairs, over both dtype plans."""
-        return sum(int(n.info.workspace_bytes) for n in self._native.values())
+        """Bytes of split-K workspace one run uses: the partial outputs o
+        (FP32 [slots, HG, GT, D]) and their (m, l) pairs, which the FP16 and
+        FP32 plans share (the larger of the two)."""
+        return max(int(n.info.workspace_bytes) for n in self._native.values())
+
+    @property
+    def device_bytes(self):
+        """Device bytes the plan holds: both dtypes' metadata and the shared workspace."""
+        return int(self._buffer.numel())
 
     @property
     def num_ctas(self):

@@ -171,7 +171,7 @@ def config4(seed=123, batch=256, low=1024, high=8192, page_size=16):
         table[b, :n] = perm[cursor:cursor + n]
         cursor += n
     layout = Layout(batch, 64, 8, 128, page_size, pool)
-    return Workload("config4_b256_gqa64x8_l1k_8k", layout, table, lengths.astype(np.int32),
+    return Workload(f"config4_b{batch}_gqa64x8_l1k_8k", layout, table, lengths.astype(np.int32),
                     256, std=0.5, seed=seed)
 
 
@@ -185,4 +185,7 @@ CONFIGS = {
     "c1": config1, "c2": config2, "c3a": lambda seed=123: config3("a", seed),
     "c3b": lambda seed=123: config3("b", seed), "c3c": lambda seed=123: config3("c", seed),
     "c4": config4, "c5": config5,
+    # config 4's generator with 32 sequences: a config-4-shaped case small
+    # enough for a full profiler capture (its traffic scales to config 4)
+    "c4s": lambda seed=123: config4(seed, batch=32),
 }

@@ -70,7 +70,8 @@ TOL = {"float16": (2e-3, 1e-3), "float32": (1e-5, 1e-5)}   # BASELINE gate (atol
 NCU_TRAFFIC_BYTES = {"c1": 67_258_880 + 571_648, "c2": 469_731_072 + 5_400_320,
                      "c3a": 2_150_068_480 + 7_169_792, "c3b": 67_789_056 + 1_476_096,
                      "c3c": 540_718_336 + 4_886_528, "c5": 1_073_953_792 + 3_577_344}
-NCU_SCALED = {}             # workload -> (captured workload, its traffic bytes)
+NCU_TRAFFIC_BYTES["c4s"] = 580_584_448 + 4_443_648
+NCU_SCALED = {"c4": ("c4s", NCU_TRAFFIC_BYTES["c4s"])}   # workload -> (captured workload, its traffic)
 
 
 def parse_args():

@@ -77,9 +77,10 @@ def csr_to_table(layout: Layout, indptr, indices, last_page_len):
 class FlashInferPlan:
     """FlashInfer's batch decode over the same NHD k/v tensors (FP16 only).
 
-    Plan construction, metadata upload and its 128 MiB workspace stay outside
-    any timing.  FlashInfer writes FP16 output; this package's decode writes
-    FP32.
+    Plan construction, metadata upload and its 1 GiB workspace stay outside
+    any timing (its tensor-core path at B256 x 64 query heads overflows the
+    usual 128 MiB).  FlashInfer writes FP16 output; this package's decode
+    writes FP32.
     """
 
     def __init__(self, layout: Layout, table, lengths, *, device="cuda", tensor_cores=False, backend="auto"):
@@ -89,7 +90,7 @@ class FlashInferPlan:
         self.version = flashinfer.__version__
         self.tensor_cores = tensor_cores
         self.backend = backend
-        self.workspace = torch.zeros(128 * 2**20, dtype=torch.uint8, device=device)
+        self.workspace = torch.zeros(2**30, dtype=torch.uint8, device=device)
         self.indptr = torch.tensor(indptr, device=device)
         self.indices = torch.tensor(indices, device=device)
         self.last = torch.tensor(last, device=device)

@@ -293,14 +293,29 @@ struct HalfEngine {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int row = mt * 16 + r8 + (mi >> 1) * 8;
+            // tokens of this lane's V^T fragment halves: a0/a1 hold c0, c0 + 1; a2/a3 c0 + 8, c0 + 9
+            const int c0 = mt * 16 + 2 * (lane & 3);
 #pragma unroll
             for (int dt = 0; dt < DT; ++dt) {
                 uint32_t a[4];
                 ldmatrix_x4_trans(a, vbase + swz128<T>(row, dt * 2 + (mi & 1)));
+                if (!full) {
+                    // Rows past the sequence end (the rest of its last page) may hold
+                    // anything, NaN included; their weight 0 must not meet them in the MMA.
+                    a[0] = mask_tokens(a[0], c0, valid);
+                    a[1] = mask_tokens(a[1], c0, valid);
+                    a[2] = mask_tokens(a[2], c0 + 8, valid);
+                    a[3] = mask_tokens(a[3], c0 + 8, valid);
+                }
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_16816(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
             }
         }
+    }
+
+    // Zero the FP16 halves of `v` (tokens tok, tok + 1) at or past `valid`.
+    static __device__ __forceinline__ uint32_t mask_tokens(uint32_t v, int tok, int valid) {
+        return tok >= valid ? 0u : (tok + 1 >= valid ? (v & 0xffffu) : v);
     }
 
     // Sum l over the 8 lanes that share each query head (lane & 3 picks the head pair).
@@ -421,26 +436,36 @@ struct FloatEngine {
             for (int i = 0; i < DPL; ++i) acc[g][i] *= alpha;
             x[g] = p;
         }
+        // Only the valid rows: the rest of a sequence's last page may hold anything
+        // (NaN included), and a zero weight times NaN is NaN.
+        if (valid >= T) {
 #pragma unroll 8
-        for (int tt = 0; tt < T; ++tt) {
-            float vv[DPL];
-            if constexpr (DPL == 2) {
-                const float2 v2 = lds_f2(vbase + swz128<T>(tt, lane >> 1) + (lane & 1) * 8);
-                vv[0] = v2.x;
-                vv[1] = v2.y;
-            } else {
-                const float4 v4 = lds_f4(vbase + swz128<T>(tt, lane));
-                vv[0] = v4.x;
-                vv[1] = v4.y;
-                vv[2] = v4.z;
-                vv[3] = v4.w;
-            }
+            for (int tt = 0; tt < T; ++tt) value_row<NH>(vbase, x, tt);
+        } else {
+            for (int tt = 0; tt < valid; ++tt) value_row<NH>(vbase, x, tt);
+        }
+    }
+
+    // acc[g] += p[g][tt] * V[tt] for the NH live heads (p[g] lives in lane tt of x[g]).
+    template <int NH>
+    __device__ __forceinline__ void value_row(uint32_t vbase, const float (&x)[NH], int tt) {
+        float vv[DPL];
+        if constexpr (DPL == 2) {
+            const float2 v2 = lds_f2(vbase + swz128<T>(tt, lane >> 1) + (lane & 1) * 8);
+            vv[0] = v2.x;
+            vv[1] = v2.y;
+        } else {
+            const float4 v4 = lds_f4(vbase + swz128<T>(tt, lane));
+            vv[0] = v4.x;
+            vv[1] = v4.y;
+            vv[2] = v4.z;
+            vv[3] = v4.w;
+        }
 #pragma unroll
-            for (int g = 0; g < NH; ++g) {
-                const float p = __shfl_sync(kFullMask, x[g], tt);
+        for (int g = 0; g < NH; ++g) {
+            const float p = __shfl_sync(kFullMask, x[g], tt);
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
-            }
+            for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(p, vv[i], acc[g][i]);
         }
     }
 

@@ -195,6 +195,34 @@ def test_tma_gather_is_bit_exact(dtype, dim, page):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("dim,page,heads,kv_heads", [(64, 16, 8, 4), (128, 16, 8, 4), (64, 32, 32, 32),
+                                                     (128, 32, 32, 1), (128, 16, 64, 8)])
+def test_rows_past_each_sequence_end_are_never_read(dtype, dim, page, heads, kv_heads):
+    # The reference reads only live tokens (decode.cu loops to the length), so
+    # whatever sits in the rest of a sequence's last page, or in a page no
+    # sequence uses, must not reach the output: fill all of it with NaN and inf.
+    lengths = [0, page * 3 + 5, page - 1, 7 * page + 1, 1]
+    layout, table, lengths = _fragmented(len(lengths), heads, kv_heads, dim, page, lengths, seed=dim + heads)
+    q, k, v = make_tensors(layout, dtype=dtype, seed=13)
+    expected = oracle(q, k, v, table, lengths)
+    live = torch.zeros((layout.physical_pages, page), dtype=torch.bool)
+    for b, n in enumerate(lengths):
+        for t in range(int(n)):
+            live[int(table[b, t // page]), t % page] = True
+    dead = ~live.to(k.device)
+    k[dead] = float("nan")
+    v[dead] = float("inf")
+    v[dead & dead[:, :1]] = float("nan")        # pages no sequence reads: NaN
+    tol = dict(atol=2e-3, rtol=1e-3) if dtype == torch.float16 else dict(atol=1e-5, rtol=1e-5)
+    for ctas in (1, 3, None):
+        plan = DecodePlan(layout, table, lengths, num_ctas=ctas)
+        out = plan.run(q, k, v).cpu().numpy()
+        assert np.isfinite(out).all()
+        np.testing.assert_allclose(out, expected, **tol)
+        assert plan.read_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_result_independent_of_cta_balance_and_repeatable(dtype):
     layout, table, lengths = _fragmented(4, 16, 4, 128, 16, [0, 33, 400, 1000], seed=21)
     q, k, v = make_tensors(layout, dtype=dtype, seed=5)

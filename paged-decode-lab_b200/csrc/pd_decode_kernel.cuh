@@ -625,13 +625,16 @@ __device__ __forceinline__ void merge_in_kernel(const DecodeArgs &a, uint8_t *sc
                                                 unsigned xe) {
     using M = RowMerge<D, HG, GT, NSUB>;
     M rm;
-    if constexpr (NC <= 4 && M::LP == 1) {
+    if constexpr ((NC <= 4 || HG == 8) && M::LP == 1) {
         if (team == 1) {
-            // Four or fewer consumer warps: each merges many rows (config 3c: ~7
-            // of ~3 partials each).  The partials of a warp's rows form one
-            // stream, U loads in flight across row boundaries, so the warp
-            // waits for one L2 round trip per U partials, not one per row.
-            // Each row still adds its partials in slot order, as fold() does.
+            // Four or fewer consumer warps, or tiles of eight KV heads: each warp
+            // merges many rows (config 3c: ~7 of ~3 partials each; config 4: ~8
+            // of 2-3).  The partials of a warp's rows form one stream, U loads in
+            // flight across row boundaries, so the warp waits for one L2 round
+            // trip per U partials, not one per row.  Each row still adds its
+            // partials in slot order, as fold() does.  (Measured: config 4 679.4
+            // -> 673.5 us, config 2 80.3 -> 81.2; the single-head eight-warp
+            // kernel of config 3b lost 1.2 us and keeps one row at a time.)
             const int K = rows > warp ? (rows - warp + NC - 1) / NC : 0;
             for (int k0 = 0; k0 < K; k0 += 32) {
                 const int kn = min(32, K - k0);

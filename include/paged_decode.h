@@ -72,7 +72,7 @@ typedef struct pd_plan_info {
     int32_t num_segments;    /* (group, page range) work segments over all CTAs */
     int32_t num_groups;      /* (sequence, KV-head group, query-head tile) groups */
     int32_t num_pieces;      /* partial slots written by the decode kernel and merged after it */
-    int32_t slot_stride;     /* partial slots reserved per segment (one per consumer sub-pipeline) */
+    int32_t slot_stride;     /* partial slots per segment (1: a CTA folds its sub-pipelines first) */
     int32_t group_tile;      /* query heads per group tile (8, 16 or 32) */
     int32_t heads_per_tile;  /* KV heads gathered per page tile (1, 2, 4 or 8) */
     int32_t total_pages;     /* page tiles streamed per decode (all groups) */

@@ -36,6 +36,7 @@
 #include <type_traits>
 
 #include "pd_device.cuh"
+#include "pd_kernels_select.hpp"
 
 namespace pd {
 
@@ -146,9 +147,17 @@ struct KernelShape {
     // the warp's own shared-memory slice (no swizzle: lanes read whole rows).
     static constexpr bool Q_SMEM = ELT != 2;
     static constexpr size_t QS = Q_SMEM ? size_t(NC) * 8 * D * ELT : 0;
-    static constexpr size_t BARS = size_t(SLOTS) * 16;
+    // With sub-pipelines, the warps of sub-pipelines 1.. hand their state for
+    // each segment to sub-pipeline 0 through shared memory: one entry each of
+    // 8 query heads' o [8][D] and (m, l) [8], and a full / free mbarrier per
+    // (head, slice) of a tile.
+    static constexpr bool FOLD = NSUB > 1 && fold_sub_pipelines(ELT, HG, GT, D, T);
+    static constexpr int CSTATES = FOLD ? NC - CPT : 0;
+    static constexpr size_t COMB_ENTRY = size_t(8) * D * 4 + 8 * 8;
+    static constexpr size_t COMB = size_t(CSTATES) * COMB_ENTRY;
+    static constexpr size_t BARS = size_t(SLOTS) * 16 + (FOLD ? size_t(CPT) * 16 : 0);
     static constexpr size_t FLAGS = size_t(SLOTS) * 4 + 16;
-    static constexpr size_t SMEM = 1024 + RING + QS + BARS + FLAGS;
+    static constexpr size_t SMEM = 1024 + RING + QS + COMB + BARS + FLAGS;
 };
 
 struct SmemFlags {
@@ -328,6 +337,31 @@ struct HalfEngine {
                 for (int s = 4; s < 32; s <<= 1) l[nt][i] += __shfl_xor_sync(kFullMask, l[nt][i], s);
     }
 
+    // After reduce(): fold in another warp's reduced state for the same query heads,
+    // o_s [heads][D] unnormalised and ml_s [heads] = (m, l), with the max-corrected
+    // merge (oracle.py:88-96); an empty state (l = 0) changes nothing.
+    __device__ __forceinline__ void absorb(const float *o_s, const float2 *ml_s) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int g = nt * 8 + 2 * (lane & 3) + i;
+                const float2 st = ml_s[g];
+                if (st.y > 0.f) {
+                    const float M = fmaxf(m[nt][i], st.x);
+                    const float a = exp2f(m[nt][i] - M), b = exp2f(st.x - M);   // a = 0 for an empty state
+                    m[nt][i] = M;
+                    l[nt][i] = fmaf(l[nt][i], a, st.y * b);
+#pragma unroll
+                    for (int dt = 0; dt < DT; ++dt) {
+                        const int d = dt * 16 + (lane >> 2);
+                        acc[dt][nt][i] = fmaf(acc[dt][nt][i], a, o_s[g * D + d] * b);
+                        acc[dt][nt][i + 2] = fmaf(acc[dt][nt][i + 2], a, o_s[g * D + d + 8] * b);
+                    }
+                }
+            }
+    }
+
     // f(g, d, o, m, l) for every accumulator element this lane holds.
     template <typename F>
     __device__ __forceinline__ void for_each_o(F &&f) const {
@@ -474,6 +508,22 @@ struct FloatEngine {
         for (int g = 0; g < GT; ++g) {
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) l[g] += __shfl_xor_sync(kFullMask, l[g], o);
+        }
+    }
+
+    // After reduce(): fold in another warp's reduced state (see HalfEngine::absorb).
+    __device__ __forceinline__ void absorb(const float *o_s, const float2 *ml_s) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+            const float2 st = ml_s[g];
+            if (st.y > 0.f) {
+                const float M = fmaxf(m[g], st.x);
+                const float a = exp2f(m[g] - M), b = exp2f(st.x - M);
+                m[g] = M;
+                l[g] = fmaf(l[g], a, st.y * b);
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(acc[g][i], a, o_s[g * D + lane * DPL + i] * b);
+            }
         }
     }
 
@@ -825,9 +875,12 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
     uint8_t *qsm = ring + S::RING;
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(qsm + S::QS);
+    float *comb = reinterpret_cast<float *>(qsm + S::QS);
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(qsm + S::QS + S::COMB);
     uint64_t *empty_bar = full_bar + SLOTS;
-    int *slot_valid = reinterpret_cast<int *>(empty_bar + SLOTS);
+    uint64_t *comb_full = empty_bar + SLOTS;            // S::FOLD: [CPT]
+    uint64_t *comb_free = comb_full + (S::FOLD ? S::CPT : 0);
+    int *slot_valid = reinterpret_cast<int *>(comb_free + (S::FOLD ? S::CPT : 0));
     SmemFlags *flags = reinterpret_cast<SmemFlags *>(slot_valid + SLOTS);
 
     const int warp = threadIdx.x >> 5;
@@ -842,6 +895,12 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         for (int s = 0; s < SLOTS; ++s) {
             mbar_init(smem_u32(full_bar + s), 1);
             mbar_init(smem_u32(empty_bar + s), S::CPT);   // released by the warps that read it
+        }
+        if constexpr (S::FOLD) {
+            for (int c = 0; c < S::CPT; ++c) {
+                mbar_init(smem_u32(comb_full + c), NSUB - 1);   // sub-pipelines 1.. posted their state
+                mbar_init(smem_u32(comb_free + c), 1);          // sub-pipeline 0 has read them
+            }
         }
         flags->abort = 0;
         mbar_init_fence();
@@ -941,6 +1000,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     const int hoff = hh * S::HEAD_BYTES;   // its head's block in each half of a tile
     bool stop = false;
     int j = 0;
+    int seg_ends = 0;                       // segments this warp has finished (handoff phases)
     const int4 sg_h = shfl_int4(hv, 1), g0_h = shfl_int4(hv, 2), g1_h = shfl_int4(hv, 3);
     for (int si = seg_begin; si < seg_end; ++si) {
         const int4 sg = si == seg_begin ? sg_h : a.segs[si];
@@ -1034,7 +1094,46 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
 
             // ---------------------------------------------------- publish this warp's state
             eng.reduce();
-            if (sg.w < 0 && a.xworld) {
+            if constexpr (S::FOLD) {
+                // Sub-pipelines 1.. post their state for this (head, slice) and go on;
+                // sub-pipeline 0 folds them in, in sub-pipeline order (so results repeat
+                // bit for bit), and writes the segment's one result.
+                const int ci = warp % S::CPT;
+                const uint32_t cf = smem_u32(comb_full + ci), cr = smem_u32(comb_free + ci);
+                bool ok = true;
+                if (sub > 0) {
+                    float *o_s = comb + size_t((sub - 1) * S::CPT + ci) * (S::COMB_ENTRY / 4);
+                    float2 *ml_s = reinterpret_cast<float2 *>(o_s + 8 * D);
+                    if (seg_ends > 0) ok = mbar_wait(cr, (seg_ends - 1) & 1);   // the last state was read
+                    if (ok) {
+                        eng.for_each_o([&](int g, int d, float o, float, float) { o_s[g * D + d] = o; });
+                        eng.for_each_ml([&](int g, float m, float l) { ml_s[g] = make_float2(m, l); });
+                    }
+                    __threadfence_block();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cf);
+                } else {
+                    ok = mbar_wait(cf, seg_ends & 1);
+                    if (ok) {
+#pragma unroll 1
+                        for (int sp = 1; sp < NSUB; ++sp) {
+                            const float *o_s = comb + size_t((sp - 1) * S::CPT + ci) * (S::COMB_ENTRY / 4);
+                            eng.absorb(o_s, reinterpret_cast<const float2 *>(o_s + 8 * D));
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cr);
+                }
+                if (!ok) {
+                    if (lane == 0) atomicOr(a.error, kErrTimeout);
+                    flags->abort = 1;
+                    stop = true;
+                }
+                ++seg_ends;
+            }
+            if (S::FOLD && sub > 0) {
+                // its state went to sub-pipeline 0
+            } else if (sg.w < 0 && a.xworld) {
                 // the final row of this rank: to its slot in every rank's exchange buffer
                 for (int x = 0; x < a.xworld; ++x) {
                     float *slot = xslot_of(a, x, xpar);
@@ -1047,7 +1146,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                 }
                 publish_rows<D>(a, qhead0, max(nw, 0), xpar, xe, lane);
             } else if (sg.w < 0) {
-                // the group's only segment and the only warp of this head: final output
+                // the group's only segment, seen whole by this CTA: final output
                 eng.for_each_o([&](int g, int d, float o, float, float l) {
                     if (g < nw) a.out[(qhead0 + g) * D + d] = l > 0.f ? o / l : 0.f;
                 });
@@ -1056,7 +1155,8 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                         if (g < nw) reinterpret_cast<float2 *>(a.stats)[qhead0 + g] = make_float2(m, l);
                     });
             } else {
-                const int64_t ps = (int64_t(sg.w) + sub) * HG + hh;   // [slot][head] partial row
+                // [slot][head] partial row: one slot per segment when folded, else one per sub-pipeline
+                const int64_t ps = (int64_t(sg.w) + (S::FOLD ? 0 : sub)) * HG + hh;
                 eng.for_each_o([&](int g, int d, float o, float, float) {
                     if (g < nw) a.part_o[(ps * GT + qt * 8 + g) * D + d] = o;
                 });
@@ -1102,7 +1202,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
             const int verdict = flags->barrier;
             // After an abort a TMA load may still be landing in the ring: no merge.
             if (!flags->abort && verdict != kBarrierLeft) {
-                merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
+                merge_in_kernel<D, HG, GT, (S::FOLD ? 1 : NSUB), NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
                 if (verdict == kBarrierGoMergeLeft) {
                     // this CTA completed the barrier after others left: merge their shares too
                     for (unsigned c = 0; c < gridDim.x; ++c) {
@@ -1111,7 +1211,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
                         int crows, cteam;
                         const int4 cmeta0 = share(c, clo, crows, cteam);
                         named_barrier_sync(1, NC * 32);   // the scratch is free again
-                        merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, clo, crows, cteam, cmeta0,
+                        merge_in_kernel<D, HG, GT, (S::FOLD ? 1 : NSUB), NC>(a, ring, warp, lane, clo, crows, cteam, cmeta0,
                                                              xpar, xe);
                     }
                     named_barrier_sync(1, NC * 32);

@@ -18,7 +18,7 @@ struct KernelEntry {
     size_t smem;
     int consumers;
     int slots;
-    int nsub;       // sub-pipelines: partial slots each segment's warps write
+    int nsub;       // sub-pipelines: partial slots each segment's warps write (1 when folded)
 };
 
 // Shape of one kernel: HG KV heads per page tile and NSUB sub-pipelines of
@@ -59,7 +59,7 @@ KernelEntry make_entry() {
     using L = LaunchShape<Elt, D, T, GT, HG>;
     using S = KernelShape<Elt, D, T, GT, HG, L::NSUB, L::SLOTS>;
     return {&paged_decode_kernel<Elt, D, T, GT, HG, L::NSUB, L::SLOTS, MODE>, S::THREADS, S::SMEM, S::NC,
-            L::SLOTS, L::NSUB};
+            L::SLOTS, S::FOLD ? 1 : L::NSUB};
 }
 
 // KV heads per tile are instantiated while an FP16 page tile (K + V of HG

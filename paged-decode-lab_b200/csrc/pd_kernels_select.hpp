@@ -37,4 +37,15 @@ inline constexpr int max_sub_pipelines(int elt, int hg, int gt, int D, int T) {
                            : (8 / tile_consumers(hg, gt) < 2 ? 8 / tile_consumers(hg, gt) : 2));
 }
 
+// Whether a kernel with sub-pipelines folds their states together inside the
+// CTA at each segment end, so that a segment writes one partial (and a group
+// that one CTA sees whole writes its output directly).  Measured against one
+// partial per sub-pipeline: the one-KV-head rank shape of config 4 on 8 GPUs
+// (8 KiB tiles, four sub-pipelines) 106.1 -> 103.2 us, FP32 config 3a 324.4 ->
+// 318.6; config 3b (two sub-pipelines of four warps, latency-bound, and two
+// fewer ring slots for the hand-off buffer) 25.4 -> 26.2, so it does not fold.
+inline constexpr bool fold_sub_pipelines(int elt, int hg, int gt, int D, int T) {
+    return max_sub_pipelines(elt, hg, gt, D, T) > 1 && (elt == 4 || max_sub_pipelines(elt, hg, gt, D, T) >= 4);
+}
+
 }  // namespace pd

@@ -188,12 +188,19 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         }
         cursor = end;
     }
-    // Partial slots.  A segment's consumer warps run as NSUB sub-pipelines
-    // (NSUB <= max_sub_pipelines(), fewer when a kernel's tiles leave room for
-    // fewer slots), each writing its own partial; slot_stride =
-    // max_sub_pipelines() slots are reserved per segment.  A group with one segment and slot_stride == 1 is
-    // seen whole by one warp per head, which writes the final output itself.
-    p.slot_stride = max_sub_pipelines(dtype == PD_FLOAT16 ? 2 : 4, hg, p.group_tile, L.head_dim, T);
+    // Partial slots.  A segment's consumer warps may run as several
+    // sub-pipelines (alternate page tiles).  Kernel shapes that fold their
+    // states inside the CTA (fold_sub_pipelines) write one partial slot per
+    // segment; the others write one per sub-pipeline, and slot_stride =
+    // max_sub_pipelines() slots are reserved per segment.  A group with one
+    // segment and slot_stride == 1 is seen whole by one CTA, which writes the
+    // final output itself.
+    {
+        const int elt = dtype == PD_FLOAT16 ? 2 : 4;
+        p.slot_stride = fold_sub_pipelines(elt, hg, p.group_tile, L.head_dim, T)
+                            ? 1
+                            : max_sub_pipelines(elt, hg, p.group_tile, L.head_dim, T);
+    }
     std::vector<int32_t> next_slot(ngroups, -1);
     int64_t slots = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) {

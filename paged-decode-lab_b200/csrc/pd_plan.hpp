@@ -50,7 +50,7 @@ struct pd_plan {
     int32_t splits = 1;
     int32_t max_context = 0;
     int32_t num_pieces = 0;        // partial slots (segments that write partials x slot_stride)
-    int32_t slot_stride = 1;       // partial slots per segment: NC0 / HG sub-pipelines
+    int32_t slot_stride = 1;       // partial slots per segment (1: sub-pipelines are folded in the CTA)
     int64_t total_pages = 0;
     int32_t sm_count = 0;          // SMs of the plan's device
     bool merge_in_kernel = false;  // split groups merged by the decode CTAs after a grid barrier

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 6
+#define PD_ABI_VERSION 7
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -84,7 +84,16 @@ typedef struct pd_plan_info {
     int32_t max_span;        /* longest sequence the work list covers (max_lengths, else lengths) */
     int64_t workspace_bytes; /* split-K partials, o and (m, l) (pd_plan_workspace_bytes) */
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
+    int32_t engine;          /* consumer engine of the decode kernel: PD_ENGINE_WARP (every
+                                consumer warp runs m16n8k16 MMAs or FP32 FMAs) or
+                                PD_ENGINE_TCGEN05 (FP16 group tiles of 32 query heads when the
+                                environment has PD_MQA_ENGINE=tcgen05 at plan creation: single
+                                threads issue the MMAs into tensor memory) */
+    int32_t reserved;
 } pd_plan_info;
+
+#define PD_ENGINE_WARP 0
+#define PD_ENGINE_TCGEN05 1
 
 /* Build a plan from host metadata.  Replaces DecodePlan.__init__'s checks and
  * split planning (runtime.py:32-69) and decode_cuda's validation

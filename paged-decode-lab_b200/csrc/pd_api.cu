@@ -23,13 +23,17 @@ const std::string &last_error();
 
 namespace {
 
-KernelEntry kernel_for(pd_dtype dtype, int D, int T, int gt, int hg, int mode) {
+KernelEntry kernel_for(pd_dtype dtype, int D, int T, int gt, int hg, int mode, int engine) {
     if (dtype == PD_FLOAT16) {
-        if (D == 64) return T == 16 ? kernel_entry_f16_d64_t16(gt, hg, mode) : kernel_entry_f16_d64_t32(gt, hg, mode);
-        return T == 16 ? kernel_entry_f16_d128_t16(gt, hg, mode) : kernel_entry_f16_d128_t32(gt, hg, mode);
+        if (D == 64)
+            return T == 16 ? kernel_entry_f16_d64_t16(gt, hg, mode, engine)
+                           : kernel_entry_f16_d64_t32(gt, hg, mode, engine);
+        return T == 16 ? kernel_entry_f16_d128_t16(gt, hg, mode, engine)
+                       : kernel_entry_f16_d128_t32(gt, hg, mode, engine);
     }
-    if (D == 64) return T == 16 ? kernel_entry_f32_d64_t16(gt, hg, mode) : kernel_entry_f32_d64_t32(gt, hg, mode);
-    return T == 16 ? kernel_entry_f32_d128_t16(gt, hg, mode) : kernel_entry_f32_d128_t32(gt, hg, mode);
+    if (D == 64)
+        return T == 16 ? kernel_entry_f32_d64_t16(gt, hg, mode, engine) : kernel_entry_f32_d64_t32(gt, hg, mode, engine);
+    return T == 16 ? kernel_entry_f32_d128_t16(gt, hg, mode, engine) : kernel_entry_f32_d128_t32(gt, hg, mode, engine);
 }
 
 std::mutex g_attr_mutex;
@@ -178,7 +182,8 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
         tc.dtype = int(dtype);
     }
     const KernelEntry e =
-        kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode);
+        kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode,
+                   p->engine);
     pd_status s = ensure_smem_attribute(p->device, e);
     if (s != PD_OK) return s;
     const auto st = static_cast<cudaStream_t>(stream);
@@ -334,6 +339,8 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->group_tile = p->group_tile;
     info->heads_per_tile = p->heads_per_tile;
     info->slot_stride = p->slot_stride;
+    info->engine = p->engine;
+    info->reserved = 0;
     info->total_pages = int32_t(p->total_pages);
     info->merge_rows = int32_t(p->merge_rows.size() / 4);
     info->merge_in_kernel = p->merge_in_kernel ? 1 : 0;

@@ -558,6 +558,93 @@ struct EngineFor<float, D, T, GT> {
 // ------------------------------------------------------------------ kernel
 enum : int { kModeDecode = 0, kModeGather = 1 };
 
+// ------------------------------------------------------------------ producer warp
+// Streams the CTA's page tiles into the ring: for each page of each segment,
+// the page's K rows, then its V rows, for the HG KV heads of the group
+// (TILE_BYTES per tile, V at +HALF_BYTES), one 5-D TMA load each, completion
+// counted on the slot's full barrier.  Slot j % SLOTS is refilled once its
+// empty barrier shows use j / SLOTS - 1 released.  Pages past a dynamic
+// plan's live length, or with an id outside the cache, land nothing and mark
+// the slot invalid.
+template <int T, int TILE_BYTES, int HALF_BYTES, int SLOTS>
+__device__ __forceinline__ void stream_page_tiles(const CUtensorMap *tm_k, const CUtensorMap *tm_v,
+                                                  const DecodeArgs &a, uint8_t *ring, uint64_t *full_bar,
+                                                  uint64_t *empty_bar, int *slot_valid, SmemFlags *flags,
+                                                  const int4 hv, int seg_begin, int seg_end, int lane) {
+    // Tiles of 8 KiB or less (one KV head, page 16) need more than one
+    // thread issuing; larger ones keep a single issuing lane (measured).
+    constexpr int PL = (TILE_BYTES <= 8192 && SLOTS >= 8) ? 4 : 1;
+    if (lane == 0) {
+        tma_prefetch_descriptor(tm_k);
+        tma_prefetch_descriptor(tm_v);
+    }
+    bool stop = false;
+    int j = 0;
+    int4 sg = shfl_int4(hv, 1), g0 = shfl_int4(hv, 2);
+    // lane i: page id of the first segment's page i (header words 16..47)
+    const int4 hp = shfl_int4(hv, 4 + (lane >> 2));
+    const int first_pages = (lane & 3) == 0 ? hp.x : (lane & 3) == 1 ? hp.y : (lane & 3) == 2 ? hp.z : hp.w;
+    for (int si = seg_begin; si < seg_end; ++si) {
+        // the next segment and its group load while this one streams
+        const bool more = si + 1 < seg_end;
+        const int4 nsg = more ? __ldg(a.segs + si + 1) : sg;
+        int4 ng0 = g0;
+        bool ng0_loaded = !more;
+        const int32_t *trow = a.table + int64_t(g0.x) * a.W;
+        const int kv0 = g0.y;
+        // dynamic plans: pages at or past the live length are skipped
+        const int live_end = a.dynamic ? max(0, a.lengths[g0.x]) : INT_MAX;
+        for (int pg = sg.y; pg < sg.z; pg += 32) {
+            const int n = min(32, sg.z - pg);
+            const int mine = (!a.dynamic && si == seg_begin && pg == sg.y)
+                                 ? first_pages
+                                 : (lane < n ? __ldg(trow + pg + lane) : 0);
+            // PL lanes issue PL consecutive tiles side by side, so one
+            // TMA instruction carries PL tiles.
+            for (int i = 0; i < n; i += PL) {
+                const int cnt = min(PL, n - i);
+                const int page = __shfl_sync(kFullMask, mine, (i + lane) & 31);
+                if (lane < cnt && !stop) {
+                    const int jj = j + lane;
+                    const int slot = jj % SLOTS;
+                    const int use = jj / SLOTS;
+                    const uint32_t fb = smem_u32(full_bar + slot);
+                    if (flags->abort ||
+                        (use > 0 && !mbar_wait(smem_u32(empty_bar + slot), (use - 1) & 1))) {
+                        if (!flags->abort) atomicOr(a.error, kErrTimeout);
+                        flags->abort = 1;
+                        stop = true;
+                    } else if (int64_t(pg + i + lane) * T >= live_end) {
+                        slot_valid[slot] = 0;   // not live yet: nothing to stream
+                        mbar_arrive(fb);
+                    } else if (page >= 0 && int64_t(page) < a.P) {
+                        slot_valid[slot] = 1;
+                        mbar_arrive_expect_tx(fb, TILE_BYTES);
+                        const uint32_t dst = smem_u32(ring + size_t(slot) * TILE_BYTES);
+                        // one instruction each for all of the page's K and V rows
+                        tma_load_5d(dst, tm_k, 0, 0, 0, kv0, page, fb);
+                        tma_load_5d(dst + HALF_BYTES, tm_v, 0, 0, 0, kv0, page, fb);
+                    } else {
+                        // The reference skips tokens whose page id is out of range
+                        // (decode.cu:58); plans validate ids, so this is defence only.
+                        atomicOr(a.error, kErrBadPage);
+                        slot_valid[slot] = 0;
+                        mbar_arrive(fb);
+                    }
+                }
+                j += cnt;
+            }
+            if (!ng0_loaded) {
+                ng0 = __ldg(a.groups + 2 * nsg.x);
+                ng0_loaded = true;
+            }
+        }
+        if (!ng0_loaded) ng0 = __ldg(a.groups + 2 * nsg.x);
+        sg = nsg;
+        g0 = ng0;
+    }
+}
+
 // ------------------------------------------------------------------ in-kernel merge
 // Runs in every CTA after the grid barrier (grid_arrive), in place
 // of the separate merge kernel.  The split groups' output rows (merge_rows,
@@ -856,6 +943,80 @@ __device__ __forceinline__ void merge_ranks(const DecodeArgs &a, int warp, int l
     }
 }
 
+// ------------------------------------------------------------------ end of a decode launch
+// After the CTA's consumer warps (0 .. NC - 1) have written every row and
+// partial of their segments: the in-kernel merge (grid barrier, then this
+// CTA's share of the split rows, with `ring` as scratch) and, in exchange
+// mode, the merge of this CTA's output rows from every rank's copies.
+// Partials were written with NSUB slots per segment.
+template <int D, int HG, int GT, int NSUB, int NC, size_t RING>
+__device__ __forceinline__ void finish_decode(const DecodeArgs &a, uint8_t *ring, SmemFlags *flags, int warp,
+                                              int lane, int xpar, uint32_t xe) {
+    if (a.fused_merge) {
+        // merge scratch, then a snapshot of the left-CTA bits (1024 bits)
+        static_assert(size_t(NC) * (D * 4 + 8) + 128 <= RING, "merge scratch must fit in the ring");
+        unsigned long long *left_snap =
+            reinterpret_cast<unsigned long long *>(ring + size_t(NC) * (D * 4 + 8));
+        // CTA c's share of the merge rows: rows [lo, lo + rows), a team of
+        // `team` warps per row when there are fewer rows than warps, and
+        // this warp's first row descriptor
+        const int64_t R = a.num_merge_rows;
+        const auto share = [&](unsigned c, int64_t &lo, int &rows, int &team) {
+            lo = R * c / gridDim.x;
+            rows = int(R * (c + 1) / gridDim.x - lo);
+            team = (rows >= NC || rows == 0) ? 1 : NC / rows;
+            const bool has = team == 1 ? warp < rows : warp < rows * team;
+            return has ? __ldg(a.merge_rows + lo + (team == 1 ? warp : warp % rows)) : make_int4(0, 0, 0, 0);
+        };
+        int64_t mlo;
+        int mrows, team;
+        const int4 meta0 = share(blockIdx.x, mlo, mrows, team);   // loads while the CTAs gather
+        named_barrier_sync(1, NC * 32);   // this CTA's partials are written
+        unsigned nleft = 0;
+        if (warp == 0 && lane == 0) {
+            const int r = grid_arrive(a.gb, gridDim.x, blockIdx.x, &nleft);
+            if (r == kBarrierTimeout) {
+                atomicOr(a.error, kErrTimeout);
+                flags->abort = 1;
+            }
+            if (r == kBarrierGoMergeLeft)
+                for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) left_snap[w] = __ldcg(a.gb.left + w);
+            flags->barrier = r;
+        }
+        named_barrier_sync(1, NC * 32);
+        const int verdict = flags->barrier;
+        // After an abort a TMA load may still be landing in the ring: no merge.
+        if (!flags->abort && verdict != kBarrierLeft) {
+            merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
+            if (verdict == kBarrierGoMergeLeft) {
+                // this CTA completed the barrier after others left: merge their shares too
+                for (unsigned c = 0; c < gridDim.x; ++c) {
+                    if (c == blockIdx.x || !((left_snap[c / 64] >> (c % 64)) & 1ull)) continue;
+                    int64_t clo;
+                    int crows, cteam;
+                    const int4 cmeta0 = share(c, clo, crows, cteam);
+                    named_barrier_sync(1, NC * 32);   // the scratch is free again
+                    merge_in_kernel<D, HG, GT, NSUB, NC>(a, ring, warp, lane, clo, crows, cteam, cmeta0,
+                                                         xpar, xe);
+                }
+                named_barrier_sync(1, NC * 32);
+                if (warp == 0 && lane == 0) {   // clear the leaves for the next launch
+                    for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) atomicAnd(a.gb.left + w, ~left_snap[w]);
+                    atomicAdd(a.gb.count, 0ull - (unsigned long long)nleft * kLeftUnit);
+                    atomicAdd(a.fallbacks, 1u);
+                }
+            }
+        }
+    }
+    if (a.xworld) {
+        // This CTA's rows are published (tagged) as they are written; merge
+        // this CTA's share of the output rows as the ranks' copies arrive.
+        if (warp == 0 && lane == 0)   // this CTA's launch count, read back by the next launch
+            reinterpret_cast<uint32_t *>(a.xpeer[a.xrank] + kXEpochs)[blockIdx.x] = xe;
+        if (!flags->abort) merge_ranks<D, NC>(a, warp, lane, xpar, xe);
+    }
+}
+
 template <typename Elt, int D, int T, int GT, int HG, int NSUB, int SLOTS, int MODE>
 __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -917,79 +1078,8 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
     const int xpar = int(xe & 1u);
 
     if (warp == NC) {
-        // ------------------------------------------------------------ producer
-        // Tiles of 8 KiB or less (one KV head, page 16) need more than one
-        // thread issuing; larger ones keep a single issuing lane (measured).
-        constexpr int PL = (S::TILE_BYTES <= 8192 && SLOTS >= 8) ? 4 : 1;
-        if (lane == 0) {
-            tma_prefetch_descriptor(&tm_k);
-            tma_prefetch_descriptor(&tm_v);
-        }
-        bool stop = false;
-        int j = 0;
-        int4 sg = shfl_int4(hv, 1), g0 = shfl_int4(hv, 2);
-        // lane i: page id of the first segment's page i (header words 16..47)
-        const int4 hp = shfl_int4(hv, 4 + (lane >> 2));
-        const int first_pages = (lane & 3) == 0 ? hp.x : (lane & 3) == 1 ? hp.y : (lane & 3) == 2 ? hp.z : hp.w;
-        for (int si = seg_begin; si < seg_end; ++si) {
-            // the next segment and its group load while this one streams
-            const bool more = si + 1 < seg_end;
-            const int4 nsg = more ? __ldg(a.segs + si + 1) : sg;
-            int4 ng0 = g0;
-            bool ng0_loaded = !more;
-            const int32_t *trow = a.table + int64_t(g0.x) * a.W;
-            const int kv0 = g0.y;
-            // dynamic plans: pages at or past the live length are skipped
-            const int live_end = a.dynamic ? max(0, a.lengths[g0.x]) : INT_MAX;
-            for (int pg = sg.y; pg < sg.z; pg += 32) {
-                const int n = min(32, sg.z - pg);
-                const int mine = (!a.dynamic && si == seg_begin && pg == sg.y)
-                                     ? first_pages
-                                     : (lane < n ? __ldg(trow + pg + lane) : 0);
-                // PL lanes issue PL consecutive tiles side by side, so one
-                // TMA instruction carries PL tiles.
-                for (int i = 0; i < n; i += PL) {
-                    const int cnt = min(PL, n - i);
-                    const int page = __shfl_sync(kFullMask, mine, (i + lane) & 31);
-                    if (lane < cnt && !stop) {
-                        const int jj = j + lane;
-                        const int slot = jj % SLOTS;
-                        const int use = jj / SLOTS;
-                        const uint32_t fb = smem_u32(full_bar + slot);
-                        if (flags->abort ||
-                            (use > 0 && !mbar_wait(smem_u32(empty_bar + slot), (use - 1) & 1))) {
-                            if (!flags->abort) atomicOr(a.error, kErrTimeout);
-                            flags->abort = 1;
-                            stop = true;
-                        } else if (int64_t(pg + i + lane) * T >= live_end) {
-                            slot_valid[slot] = 0;   // not live yet: nothing to stream
-                            mbar_arrive(fb);
-                        } else if (page >= 0 && int64_t(page) < a.P) {
-                            slot_valid[slot] = 1;
-                            mbar_arrive_expect_tx(fb, S::TILE_BYTES);
-                            const uint32_t dst = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
-                            // one instruction each for all of the page's K and V rows
-                            tma_load_5d(dst, &tm_k, 0, 0, 0, kv0, page, fb);
-                            tma_load_5d(dst + S::HALF_BYTES, &tm_v, 0, 0, 0, kv0, page, fb);
-                        } else {
-                            // The reference skips tokens whose page id is out of range
-                            // (decode.cu:58); plans validate ids, so this is defence only.
-                            atomicOr(a.error, kErrBadPage);
-                            slot_valid[slot] = 0;
-                            mbar_arrive(fb);
-                        }
-                    }
-                    j += cnt;
-                }
-                if (!ng0_loaded) {
-                    ng0 = __ldg(a.groups + 2 * nsg.x);
-                    ng0_loaded = true;
-                }
-            }
-            if (!ng0_loaded) ng0 = __ldg(a.groups + 2 * nsg.x);
-            sg = nsg;
-            g0 = ng0;
-        }
+        stream_page_tiles<T, S::TILE_BYTES, S::HALF_BYTES, SLOTS>(&tm_k, &tm_v, a, ring, full_bar, empty_bar,
+                                                                slot_valid, flags, hv, seg_begin, seg_end, lane);
         return;
     }
 
@@ -1167,69 +1257,7 @@ __global__ void __launch_bounds__((HG * (GT / 8) * NSUB + 1) * 32, 1)
         }
     }
     if constexpr (MODE == kModeDecode) {
-        if (a.fused_merge) {
-            // merge scratch, then a snapshot of the left-CTA bits (1024 bits)
-            static_assert(size_t(NC) * (D * 4 + 8) + 128 <= S::RING, "merge scratch must fit in the ring");
-            unsigned long long *left_snap =
-                reinterpret_cast<unsigned long long *>(ring + size_t(NC) * (D * 4 + 8));
-            // CTA c's share of the merge rows: rows [lo, lo + rows), a team of
-            // `team` warps per row when there are fewer rows than warps, and
-            // this warp's first row descriptor
-            const int64_t R = a.num_merge_rows;
-            const auto share = [&](unsigned c, int64_t &lo, int &rows, int &team) {
-                lo = R * c / gridDim.x;
-                rows = int(R * (c + 1) / gridDim.x - lo);
-                team = (rows >= NC || rows == 0) ? 1 : NC / rows;
-                const bool has = team == 1 ? warp < rows : warp < rows * team;
-                return has ? __ldg(a.merge_rows + lo + (team == 1 ? warp : warp % rows)) : make_int4(0, 0, 0, 0);
-            };
-            int64_t mlo;
-            int mrows, team;
-            const int4 meta0 = share(blockIdx.x, mlo, mrows, team);   // loads while the CTAs gather
-            named_barrier_sync(1, NC * 32);   // this CTA's partials are written
-            unsigned nleft = 0;
-            if (warp == 0 && lane == 0) {
-                const int r = grid_arrive(a.gb, gridDim.x, blockIdx.x, &nleft);
-                if (r == kBarrierTimeout) {
-                    atomicOr(a.error, kErrTimeout);
-                    flags->abort = 1;
-                }
-                if (r == kBarrierGoMergeLeft)
-                    for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) left_snap[w] = __ldcg(a.gb.left + w);
-                flags->barrier = r;
-            }
-            named_barrier_sync(1, NC * 32);
-            const int verdict = flags->barrier;
-            // After an abort a TMA load may still be landing in the ring: no merge.
-            if (!flags->abort && verdict != kBarrierLeft) {
-                merge_in_kernel<D, HG, GT, (S::FOLD ? 1 : NSUB), NC>(a, ring, warp, lane, mlo, mrows, team, meta0, xpar, xe);
-                if (verdict == kBarrierGoMergeLeft) {
-                    // this CTA completed the barrier after others left: merge their shares too
-                    for (unsigned c = 0; c < gridDim.x; ++c) {
-                        if (c == blockIdx.x || !((left_snap[c / 64] >> (c % 64)) & 1ull)) continue;
-                        int64_t clo;
-                        int crows, cteam;
-                        const int4 cmeta0 = share(c, clo, crows, cteam);
-                        named_barrier_sync(1, NC * 32);   // the scratch is free again
-                        merge_in_kernel<D, HG, GT, (S::FOLD ? 1 : NSUB), NC>(a, ring, warp, lane, clo, crows, cteam, cmeta0,
-                                                             xpar, xe);
-                    }
-                    named_barrier_sync(1, NC * 32);
-                    if (warp == 0 && lane == 0) {   // clear the leaves for the next launch
-                        for (unsigned w = 0; w < (gridDim.x + 63) / 64; ++w) atomicAnd(a.gb.left + w, ~left_snap[w]);
-                        atomicAdd(a.gb.count, 0ull - (unsigned long long)nleft * kLeftUnit);
-                        atomicAdd(a.fallbacks, 1u);
-                    }
-                }
-            }
-        }
-        if (a.xworld) {
-            // This CTA's rows are published (tagged) as they are written; merge
-            // this CTA's share of the output rows as the ranks' copies arrive.
-            if (warp == 0 && lane == 0)   // this CTA's launch count, read back by the next launch
-                reinterpret_cast<uint32_t *>(a.xpeer[a.xrank] + kXEpochs)[blockIdx.x] = xe;
-            if (!flags->abort) merge_ranks<D, NC>(a, warp, lane, xpar, xe);
-        }
+        finish_decode<D, HG, GT, (S::FOLD ? 1 : NSUB), NC, S::RING>(a, ring, flags, warp, lane, xpar, xe);
         if (a.fused_merge || a.xworld) return;
     }
     // Let the dependent merge kernel launch; it still waits for this grid to finish.

@@ -1,0 +1,616 @@
+// pd_decode_mqa.cuh — the decode kernel for wide query groups (MQA-like:
+// 17..32 query heads per KV head, FP16) on the 5th-generation tensor cores.
+//
+// Same work list, page-tile ring, partials and merges as paged_decode_kernel
+// (pd_decode_kernel.cuh; the reference's partial_decode + merge in
+// src/paged_decode/csrc/decode.cu:26-168), with the consumer side rebuilt
+// around tcgen05:
+//
+//   * warp 7 (producer) streams page tiles (K then V of one page of one KV
+//     head) into the ring with TMA, as in the warp-level kernel;
+//   * warp 2 stages each segment's 32 query rows in shared memory (128-byte
+//     swizzled, K-major) two segments ahead;
+//   * one thread of warp 3 issues S = Q K^T for each page as it lands (M = 64
+//     rows of which the 32 query heads are 0..31, N = page tokens, K = head
+//     dim) into a double-buffered score block in tensor memory; one thread of
+//     warp 6, once a step's weights P are in shared memory, issues O += P V
+//     (N = head dim) and L += P 1 (the softmax denominators: the FP16 weights
+//     summed by the tensor core in FP32) into an output block in tensor
+//     memory.  Two issuing threads, so that neither kind waits for the other's
+//     inputs (pages landing, weights written);
+//   * warps 0 and 4 own query heads 0..15, warps 1 and 5 heads 16..31
+//     (tensor-memory lanes 0..15 of sub-partitions 0 and 1); of each step's
+//     NS score columns a warp takes one half, two threads per head.  Online
+//     softmax in base 2 with a lazily moved reference maximum: the two warps
+//     of a head trade their row maxima each step, and only a maximum that
+//     passes the reference by more than 2^8 moves it (and rescales the output
+//     block), so weights stay <= 256 in FP16.  At each segment end the output
+//     block comes back from tensor memory and is written out exactly as the
+//     warp-level kernel writes it (final row, exchange row or (m, l, o)
+//     partial, m the true maximum).
+//
+// A step is NP consecutive pages of one segment (NS = NP * T score columns).
+// mbarriers order the roles: ring full/empty (TMA -> MMA), q_full/q_empty
+// (query rows), s_full (scores ready), p_full (weights written), p_free (the
+// step's PV products done: its weights and ring slots are free, the output
+// block quiescent), o_free (a segment's output read back), pair (the two
+// softmax warps of the same heads).  Every wait is bounded; on a timeout the
+// CTA records PD_DEVERR_TIMEOUT, unwinds, waits for its own MMAs and frees its
+// tensor memory.
+#pragma once
+
+#include "pd_decode_kernel.cuh"
+#include "pd_tcgen05.cuh"
+
+namespace pd {
+
+template <int D, int T>
+struct MqaShape {
+    static constexpr int GT = 32;                       // query heads of a group tile: MMA rows 0..31
+    // warps 0..6 (all merge at the end), warp 7 produces: eight warps, two per
+    // SM sub-partition, so each thread may hold up to 255 registers
+    static constexpr int NC = 7;
+    static constexpr int THREADS = (NC + 1) * 32;
+    static constexpr int W_Q = 2, W_MMA = 3, W_PV = 6;  // softmax: warps 0, 1, 4, 5
+    static constexpr int M = 64;                        // MMA rows (the smallest cta_group::1 shape)
+    static constexpr int ROW_BYTES = D * 2;
+    static constexpr int NBOX = ROW_BYTES / 128;        // 128-byte boxes per token row
+    static constexpr int HALF_BYTES = NBOX * T * 128;   // K (or V) rows of one page: [box][token]
+    static constexpr int TILE_BYTES = 2 * HALF_BYTES;
+    static constexpr int NS = 128;                      // score columns per step
+    static constexpr int NP = NS / T;                   // pages per step
+    static constexpr int KSTEPS = D / 16;               // K = 16 MMAs of S = Q K^T
+    static constexpr int PSTEPS = T / 16;               // K = 16 MMAs of O += P V per page
+    static constexpr int OCW = D / 64;                  // 32-column output blocks per softmax warp
+    static constexpr int CW = NS / 64;                  // 32-column score blocks per softmax warp and step
+    static constexpr int Q_BOX = GT * 128;              // one 128-byte box of the 32 query rows
+    static constexpr int Q_BYTES = NBOX * Q_BOX;
+    static constexpr int P_SBO = NS * 16;               // 8 rows of NS FP16 weights (8x8 core matrices)
+    static constexpr int P_BYTES = (GT / 8) * P_SBO;
+    static constexpr int ONES_BYTES = 512;              // B = 1 (16 tokens x 16 columns) for L += P 1
+    // An M = 64 MMA reads 64 rows of A; rows 32..63 (never read back from
+    // tensor memory) come from whatever follows the 32 written rows, which
+    // must be allocated shared memory: P buffer 1 reads on into the Q
+    // buffers, Q buffer 1 into GUARD bytes after them.
+    static constexpr int P_READ = (M / 8) * P_SBO;                      // from a P buffer's start
+    static constexpr int Q_READ = (NBOX - 1) * Q_BOX + (M / 8) * 1024;  // from a Q buffer's start
+    static constexpr int GUARD = Q_READ > Q_BYTES ? Q_READ - Q_BYTES : 0;
+    // tensor-memory columns: O block [0, D), L block [D, D + 32) (16 written),
+    // score blocks [S_COL, S_COL + NS), [S_COL + NS, S_COL + 2 NS)
+    static constexpr int O_COL = 0;
+    static constexpr int L_COL = D;
+    static constexpr int S_COL = D + 32;
+    static constexpr int TMEM_COLS = (S_COL + 2 * NS) <= 256 ? 256 : 512;
+    static constexpr int NBARS = 18;   // s_full, p_full, p_free, q_full, q_empty: 2 each; pair: 4; o_free; mma_done: 2
+    static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] floats
+    static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + GUARD + ONES_BYTES +
+                                    NBARS * 8 + XMAX_BYTES + 16 + 16 + 16;
+    static constexpr int FIT = int((232448 - FIXED) / (TILE_BYTES + 8 + 8 + 4));
+    static constexpr int SLOTS = FIT > 32 ? 32 : FIT;
+    static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
+    static constexpr size_t SMEM = FIXED + RING + size_t(SLOTS) * 20;
+
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    static_assert(T == 16 || T == 32, "page_size 16 or 32");
+    static_assert(NS == 64 || NS == 128, "a step is 64 or 128 score columns");
+    static_assert(P_READ <= P_BYTES + 2 * Q_BYTES, "P buffer 1's unread rows must stay inside the Q buffers");
+    static_assert(S_COL + 2 * NS <= TMEM_COLS, "tensor memory budget");
+    // a step's slots are released after its PV products: the ring must hold
+    // two steps at once, and then some to stream ahead
+    static_assert(SLOTS >= 2 * NP + 2, "ring too small for two steps in flight");
+    static_assert(SMEM <= 232448 && SMEM > 116 * 1024,
+                  "one CTA per SM: its tensor memory is never contended by a second CTA of the grid");
+};
+
+// One thread's share of an output row: columns c0 + 32c + 16 half + [0, 16)
+// (c < OCW) of the tensor-memory output block, scaled, as float4 stores.
+template <int OCW>
+__device__ __forceinline__ void store_o_part(float *dst, const uint32_t (&ov)[OCW][16], int c0, int half,
+                                             float scale) {
+#pragma unroll
+    for (int c = 0; c < OCW; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(dst + c0 + 32 * c + 16 * half + e) =
+                make_float4(__uint_as_float(ov[c][e]) * scale, __uint_as_float(ov[c][e + 1]) * scale,
+                            __uint_as_float(ov[c][e + 2]) * scale, __uint_as_float(ov[c][e + 3]) * scale);
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x (hardware approximation; results below 2^-126 flush to 0, which FP16
+// weights could not hold anyway).
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+template <int D, int T>
+__global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
+    paged_decode_mqa_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                            const DecodeArgs a) {
+    using S = MqaShape<D, T>;
+    constexpr int NC = S::NC, NS = S::NS, NP = S::NP, SLOTS = S::SLOTS, GT = S::GT, OCW = S::OCW, CW = S::CW;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem;
+    uint8_t *pbuf = ring + S::RING;
+    uint8_t *qbuf = pbuf + 2 * S::P_BYTES;
+    uint8_t *ones = qbuf + 2 * S::Q_BYTES + S::GUARD;
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(ones + S::ONES_BYTES);
+    uint64_t *empty_bar = full_bar + SLOTS;
+    uint64_t *s_full = empty_bar + SLOTS;   // [2] per score block
+    uint64_t *p_full = s_full + 2;          // [2] per weight buffer
+    uint64_t *p_free = p_full + 2;          // [2]
+    uint64_t *q_full = p_free + 2;          // [2] per query buffer
+    uint64_t *q_empty = q_full + 2;         // [2]
+    uint64_t *pair_bar = q_empty + 2;       // [2 heads halves][2 phases]
+    uint64_t *o_free = pair_bar + 4;
+    uint64_t *mma_done = o_free + 1;        // [2] score MMAs, PV MMAs
+    float *xmax = reinterpret_cast<float *>(mma_done + 2);
+    unsigned *svalid = reinterpret_cast<unsigned *>(xmax + S::XMAX_BYTES / 4);   // [2]: pages streamed, per score block
+    int *slot_valid = reinterpret_cast<int *>(svalid + 4);
+    SmemFlags *flags = reinterpret_cast<SmemFlags *>(slot_valid + SLOTS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(flags + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int4 hv = lane < 12 ? __ldg(a.head + int64_t(blockIdx.x) * 16 + lane) : make_int4(0, 0, 0, 0);
+    const int seg_begin = __shfl_sync(kFullMask, hv.x, 0);
+    const int seg_end = __shfl_sync(kFullMask, hv.y, 0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SLOTS; ++s) {
+            mbar_init(smem_u32(full_bar + s), 1);
+            mbar_init(smem_u32(empty_bar + s), 1);   // one commit of the MMA thread
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(s_full + b), 2);      // the scores' commit and the MMA thread (svalid)
+            mbar_init(smem_u32(p_full + b), 4);      // the four softmax warps
+            mbar_init(smem_u32(p_free + b), 1);
+            mbar_init(smem_u32(q_full + b), 1);
+            mbar_init(smem_u32(q_empty + b), 1);
+        }
+        for (int i = 0; i < 4; ++i) mbar_init(smem_u32(pair_bar + i), 2);
+        mbar_init(smem_u32(o_free), 4);
+        mbar_init(smem_u32(mma_done), 1);
+        mbar_init(smem_u32(mma_done + 1), 1);
+        flags->abort = 0;
+        mbar_init_fence();
+    }
+    if (warp == S::W_MMA) {
+        tc::alloc(smem_u32(tmem_slot), S::TMEM_COLS);
+        tc::relinquish_alloc_permit();
+        tc::fence_before_sync();
+    }
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (a.fused_merge && threadIdx.x == 0) atomicAdd(a.gb.started, 1ull);
+    const uint32_t xe = a.xworld
+        ? __ldcv(reinterpret_cast<const unsigned int *>(a.xpeer[a.xrank] + kXEpochs) + blockIdx.x) + 1u : 0u;
+    const int xpar = int(xe & 1u);
+
+    if (warp == NC) {
+        stream_page_tiles<T, S::TILE_BYTES, S::HALF_BYTES, SLOTS>(&tm_k, &tm_v, a, ring, full_bar, empty_bar,
+                                                                slot_valid, flags, hv, seg_begin, seg_end, lane);
+        return;
+    }
+
+    const auto fail_wait = [&]() {
+        if (!flags->abort) atomicOr(a.error, kErrTimeout);
+        flags->abort = 1;
+    };
+    // A whole warp waits and decides together (a timed-out lane must not
+    // leave its warp diverged at the next warp-wide instruction).
+    const auto warp_wait = [&](uint64_t *bar, int parity) {
+        return __all_sync(kFullMask, mbar_wait(smem_u32(bar), uint32_t(parity)));
+    };
+    const auto warp_abort = [&]() { return __any_sync(kFullMask, flags->abort != 0); };
+    const int4 sg_h = shfl_int4(hv, 1), g0_h = shfl_int4(hv, 2), g1_h = shfl_int4(hv, 3);
+
+    if (warp == S::W_Q) {
+        // ------------------------------------------------------------ query rows
+        // B = 1 for L += P 1, once: 16 x 16 FP16 ones in 8x8 core matrices.
+        for (int e = lane; e < S::ONES_BYTES / 16; e += 32)
+            reinterpret_cast<uint4 *>(ones)[e] = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+        // Segment sc (counting segments with pages) goes to buffer sc % 2 once
+        // the score MMAs of segment sc - 2 are done: row g of the tile at
+        // [box][row][128 B], 16-byte chunks XORed by row % 8 (the layout the
+        // 128-byte-swizzle descriptor reads); rows past the group's heads are zero.
+        int sc = 0;
+        for (int si = seg_begin; si < seg_end && !warp_abort(); ++si) {
+            const int4 sg = si == seg_begin ? sg_h : a.segs[si];
+            if (sg.z == sg.y) continue;
+            const int4 g0 = si == seg_begin ? g0_h : a.groups[2 * sg.x];
+            const int qb = sc & 1;
+            if (sc >= 2 && !warp_wait(q_empty + qb, ((sc >> 1) - 1) & 1)) {
+                if (lane == 0) fail_wait();
+                break;
+            }
+            const int nh = g0.w;
+            const __half *qrow = static_cast<const __half *>(a.q) +
+                                 (int64_t(g0.x) * a.Hq + int64_t(g0.y) * a.group + g0.z) * D;
+            uint8_t *qs = qbuf + qb * S::Q_BYTES;
+            constexpr int CPR = D / 8;   // 16-byte chunks per row
+#pragma unroll 4
+            for (int e = lane; e < GT * CPR; e += 32) {
+                const int row = e / CPR, c = e % CPR;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (row < nh) v = __ldg(reinterpret_cast<const uint4 *>(qrow + int64_t(row) * D) + c);
+                *reinterpret_cast<uint4 *>(qs + swz128<GT>(row, c)) = v;
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(q_full + qb));
+            ++sc;
+        }
+    } else if (warp == S::W_MMA) {
+        // ------------------------------------------------------------ score MMAs (one thread)
+        // S = Q K^T for each page as it lands, into score block gs % 2 once the
+        // weights of step gs - 2 (which read that block) are written.
+        if (lane == 0) {
+            constexpr uint32_t ID_S = tc::idesc_f16_f32(S::M, T, false, false);   // Q, K: K-major
+            bool stop = false;
+            int gs = 0, j = 0, sc = 0;
+            for (int si = seg_begin; si < seg_end && !stop; ++si) {
+                const int4 sg = si == seg_begin ? sg_h : a.segs[si];
+                const int npg = sg.z - sg.y;
+                if (npg == 0) continue;
+                const int qb = sc & 1;
+                if (!mbar_wait(smem_u32(q_full + qb), (sc >> 1) & 1)) {
+                    stop = true;
+                    break;
+                }
+                const uint32_t qa = smem_u32(qbuf + qb * S::Q_BYTES);
+                for (int p0 = 0; p0 < npg; p0 += NP) {
+                    const int n = min(NP, npg - p0);
+                    const int b = gs & 1;
+                    if (flags->abort || (gs >= 2 && !mbar_wait(smem_u32(p_full + b), ((gs >> 1) - 1) & 1))) {
+                        stop = true;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    unsigned valid = 0;
+                    for (int p = 0; p < n; ++p) {
+                        const int jj = j + p;
+                        const int slot = jj % SLOTS;
+                        if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
+                            stop = true;
+                            break;
+                        }
+                        if (!slot_valid[slot]) continue;
+                        valid |= 1u << p;
+                        const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < S::KSTEPS; ++kk) {
+                            const uint32_t koff = (kk >> 2) * (T * 128) + (kk & 3) * 32;
+                            const uint64_t ad = tc::smem_desc(qa + (kk >> 2) * S::Q_BOX + (kk & 3) * 32, 16, 1024,
+                                                              tc::kSwizzle128);
+                            const uint64_t bd = tc::smem_desc(kb + koff, 16, 1024, tc::kSwizzle128);
+                            tc::mma_f16(tmem + S::S_COL + b * NS + p * T, ad, bd, ID_S, kk > 0 ? 1u : 0u);
+                        }
+                    }
+                    if (stop) break;
+                    tc::commit(smem_u32(s_full + b));
+                    svalid[b] = valid;
+                    mbar_arrive(smem_u32(s_full + b));
+                    if (p0 + NP >= npg) tc::commit(smem_u32(q_empty + qb));   // the segment's query rows
+                    ++gs;
+                    j += n;
+                }
+                ++sc;
+            }
+            if (stop) fail_wait();
+            // every score MMA has finished before the ring is reused or freed
+            tc::commit(smem_u32(mma_done));
+            if (!mbar_wait(smem_u32(mma_done), 0)) fail_wait();
+        }
+        __syncwarp();
+    } else if (warp == S::W_PV) {
+        // ------------------------------------------------------------ PV MMAs (one thread)
+        // Once a step's weights are written: O += P V and L += P 1 (a segment's
+        // first product overwrites, after the previous segment's output block
+        // was read back), then commits that free the weight buffer and the
+        // step's ring slots.
+        if (lane == 0) {
+            constexpr uint32_t ID_O = tc::idesc_f16_f32(S::M, D, false, true);    // P K-major, V MN-major
+            constexpr uint32_t ID_L = tc::idesc_f16_f32(S::M, 16, false, false);  // P, ones: K-major
+            const uint64_t ones_desc = tc::smem_desc(smem_u32(ones), 128, 256, tc::kNoSwizzle);
+            bool stop = false;
+            int gs = 0, j = 0, sc = 0;
+            for (int si = seg_begin; si < seg_end && !stop; ++si) {
+                const int4 sg = si == seg_begin ? sg_h : a.segs[si];
+                const int npg = sg.z - sg.y;
+                if (npg == 0) continue;
+                uint32_t accumulate = 0;
+                for (int p0 = 0; p0 < npg; p0 += NP) {
+                    const int n = min(NP, npg - p0);
+                    const int b = gs & 1;
+                    if (!mbar_wait(smem_u32(p_full + b), (gs >> 1) & 1) ||
+                        (p0 == 0 && sc > 0 && !mbar_wait(smem_u32(o_free), (sc - 1) & 1))) {
+                        stop = true;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t pb = smem_u32(pbuf + b * S::P_BYTES);
+                    for (int p = 0; p < n; ++p) {
+                        const int jj = j + p;
+                        const int slot = jj % SLOTS;
+                        if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {   // seen already
+                            stop = true;
+                            break;
+                        }
+                        if (!slot_valid[slot]) continue;
+                        const uint32_t vb = smem_u32(ring + size_t(slot) * S::TILE_BYTES) + S::HALF_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < S::PSTEPS; ++kk) {
+                            const uint64_t ad =
+                                tc::smem_desc(pb + (p * S::PSTEPS + kk) * 256, 128, S::P_SBO, tc::kNoSwizzle);
+                            const uint64_t bd = tc::smem_desc(vb + kk * 16 * 128, T * 128, 1024, tc::kSwizzle128);
+                            tc::mma_f16(tmem + S::O_COL, ad, bd, ID_O, accumulate);
+                            tc::mma_f16(tmem + S::L_COL, ad, ones_desc, ID_L, accumulate);
+                            accumulate = 1;
+                        }
+                    }
+                    if (stop) break;
+                    tc::commit(smem_u32(p_free + b));
+                    for (int p = 0; p < n; ++p) tc::commit(smem_u32(empty_bar + (j + p) % SLOTS));
+                    ++gs;
+                    j += n;
+                }
+                ++sc;
+            }
+            if (stop) fail_wait();
+            tc::commit(smem_u32(mma_done + 1));
+            if (!mbar_wait(smem_u32(mma_done + 1), 0)) fail_wait();
+        }
+        __syncwarp();
+    } else if (warp == 0 || warp == 1 || warp == 4 || warp == 5) {
+        // ------------------------------------------------------------ softmax
+        const int quad = warp & 3;                  // heads 16 quad .. + 15: TMEM lanes of sub-partition quad
+        const int cs = warp >> 2;                   // which half of a step's score columns (and of O)
+        const int hrow = 16 * quad + (lane & 15);   // query head of the tile (MMA row)
+        const int half = lane >> 4;                 // which 16 of each 32 columns
+        const uint32_t tl = tmem + (uint32_t(32 * quad) << 16);   // this warp's lane sub-partition
+        const int c0 = cs * (NS / 2);               // first score column of this warp
+        const int oc0 = cs * (D / 2);               // first output column of this warp
+        // The two warps of the same heads meet through pair_bar[quad][n % 2]
+        // (n counts their meetings); row maxima travel through
+        // xmax[n % 2][quad][cs][row].
+        int npair = 0;
+        const auto pair_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(pair_bar + quad * 2 + (npair & 1)));
+            const bool ok = warp_wait(pair_bar + quad * 2 + (npair & 1), (npair >> 1) & 1);
+            ++npair;
+            return ok;
+        };
+        int gs = 0, j = 0;
+        bool stop = false;
+        for (int si = seg_begin; si < seg_end; ++si) {
+            const int4 sg = si == seg_begin ? sg_h : a.segs[si];
+            const int4 g0 = si == seg_begin ? g0_h : a.groups[2 * sg.x];
+            const int4 g1 = si == seg_begin ? g1_h : a.groups[2 * sg.x + 1];
+            const int nh = g0.w;
+            int length = g1.x;
+            if (a.dynamic) {
+                const int live = a.lengths[g0.x];
+                if (live > length && warp == 0 && lane == 0) atomicOr(a.error, kErrLength);
+                length = min(max(live, 0), length);
+            }
+            const int npg = sg.z - sg.y;
+            float m_ref = -INFINITY;   // the maximum the weights are taken against
+            float m_top = -INFINITY;   // the true running maximum
+            bool o_live = false;       // a PV product has been issued in this segment
+            uint32_t ov[OCW][16];      // this warp's part of the output row at the segment end
+            float l = 0.f;
+            if (npg > 0 && !stop) {
+                for (int p0 = 0; p0 < npg; p0 += NP) {
+                    const int n = min(NP, npg - p0);
+                    const int b = gs & 1;
+                    if (warp_abort() || !warp_wait(s_full + b, (gs >> 1) & 1)) {
+                        stop = true;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    uint32_t sv[CW][16];
+#pragma unroll
+                    for (int c = 0; c < CW; ++c) tc::ld_16x32bx2_x16(tl + S::S_COL + b * NS + c0 + 32 * c, sv[c]);
+                    const unsigned valid = svalid[b];   // written before the MMA thread's arrive
+                    tc::wait_ld();
+                    // mask pages not streamed and tokens past the end (raw scores: the scale is > 0)
+                    const int tok0 = (sg.y + p0) * T;
+                    if (!(n == NP && valid == (1u << NP) - 1u && tok0 + NS <= length)) {
+#pragma unroll
+                        for (int c = 0; c < CW; ++c)
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const int col = c0 + 32 * c + 16 * half + e;
+                                if (!(col < n * T && ((valid >> (col / T)) & 1u) && tok0 + col < length))
+                                    sv[c][e] = __float_as_uint(-INFINITY);
+                            }
+                    }
+                    // this thread's maximum (a tree of 3-input maxima), then the row's over both warps
+                    float t4[4 * CW];
+#pragma unroll
+                    for (int i = 0; i < 4 * CW; ++i) {
+                        const uint32_t *x = &sv[i >> 2][(i & 3) * 4];
+                        t4[i] = max3f(__uint_as_float(x[0]), __uint_as_float(x[1]),
+                                      fmaxf(__uint_as_float(x[2]), __uint_as_float(x[3])));
+                    }
+                    float mloc = fmaxf(max3f(t4[0], t4[1], t4[2]), t4[3]);
+                    if constexpr (CW == 2) mloc = fmaxf(mloc, fmaxf(max3f(t4[4], t4[5], t4[6]), t4[7]));
+                    mloc = fmaxf(mloc, __shfl_xor_sync(kFullMask, mloc, 16));
+                    float *xm = xmax + (npair & 1) * 64 + quad * 32;
+                    if (half == 0) xm[cs * 16 + (lane & 15)] = mloc;
+                    if (!pair_sync()) {
+                        stop = true;
+                        break;
+                    }
+                    const float mx = fmaxf(mloc, xm[(cs ^ 1) * 16 + (lane & 15)]) * a.scale_log2;
+                    m_top = fmaxf(m_top, mx);
+                    const bool grow = mx > m_ref + 8.f;
+                    float alpha = 1.f;
+                    if (grow) {
+                        alpha = ex2_ftz(m_ref - mx);   // 0 while nothing was seen
+                        m_ref = mx;
+                    }
+                    const float nu = m_ref == -INFINITY ? 0.f : -m_ref;
+                    // weight buffer b is free once the PV products of step gs - 2 are done
+                    if (gs >= 2 && !warp_wait(p_free + b, ((gs >> 1) - 1) & 1)) {
+                        stop = true;
+                        break;
+                    }
+                    // row hrow, tokens c0 + 32c + 16 half + [0, 16): two 8x8 core matrices
+                    const uint32_t prow = smem_u32(pbuf + b * S::P_BYTES) + (hrow & 7) * 16 + (hrow >> 3) * S::P_SBO;
+#pragma unroll
+                    for (int c = 0; c < CW; ++c) {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            w[e] = pack_half2(ex2_ftz(fmaf(__uint_as_float(sv[c][2 * e]), a.scale_log2, nu)),
+                                              ex2_ftz(fmaf(__uint_as_float(sv[c][2 * e + 1]), a.scale_log2, nu)));
+                        const uint32_t at = prow + ((c0 + 32 * c + 16 * half) >> 3) * 128;
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(at), "r"(w[0]), "r"(w[1]),
+                                     "r"(w[2]), "r"(w[3]) : "memory");
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(at + 128), "r"(w[4]),
+                                     "r"(w[5]), "r"(w[6]), "r"(w[7]) : "memory");
+                    }
+                    // V rows past the sequence end in its last page may hold anything,
+                    // NaN included; their weight 0 must not meet them in the MMA.
+                    if (quad == 0) {
+                        const int pz = (length - tok0) / T;
+                        const int vt = (length - tok0) - pz * T;
+                        if (length > tok0 && pz < n && vt > 0 && ((valid >> pz) & 1u)) {
+                            // the page's load landed (seen here too, before writing over it)
+                            if (!warp_wait(full_bar + (j + pz) % SLOTS, ((j + pz) / SLOTS) & 1)) {
+                                stop = true;
+                                break;
+                            }
+                            uint8_t *vrows = ring + size_t((j + pz) % SLOTS) * S::TILE_BYTES + S::HALF_BYTES;
+                            constexpr int UPR = S::NBOX * 8;   // 16-byte units per token row
+                            for (int e = cs * 32 + lane; e < (T - vt) * UPR; e += 64) {
+                                const int row = vt + e / UPR, u16 = e % UPR;
+                                *reinterpret_cast<uint4 *>(vrows + (u16 >> 3) * (T * 128) + row * 128 + (u16 & 7) * 16) =
+                                    make_uint4(0u, 0u, 0u, 0u);
+                            }
+                        }
+                    }
+                    // A moved reference rescales what the earlier steps built: the two
+                    // warps of these heads see the same maxima, so both take this branch
+                    // (each its part of the output block, warp cs = 1 also the L block).
+                    if (__any_sync(kFullMask, grow && o_live)) {
+                        if (!warp_wait(p_free + ((gs - 1) & 1), ((gs - 1) >> 1) & 1)) {
+                            stop = true;
+                            break;
+                        }
+                        tc::fence_after_sync();
+#pragma unroll
+                        for (int c = 0; c <= OCW; ++c) {
+                            if (c == OCW && cs == 0) break;
+                            const uint32_t col = c < OCW ? S::O_COL + oc0 + 32 * c : S::L_COL;
+                            uint32_t r[16];
+                            tc::ld_16x32bx2_x16(tl + col, r);
+                            tc::wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                            tc::st_16x32bx2_x16(tl + col, r);
+                        }
+                        tc::wait_st();
+                    }
+                    o_live = o_live || valid != 0u;
+                    tc::fence_proxy_async_smem();
+                    tc::fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(p_full + b));
+                    ++gs;
+                    j += n;
+                }
+                // the segment's output block, once its last PV products are done
+                if (!stop && o_live) {
+                    if (!warp_wait(p_free + ((gs - 1) & 1), ((gs - 1) >> 1) & 1)) {
+                        stop = true;
+                    } else {
+                        tc::fence_after_sync();
+                        uint32_t lv[16];
+#pragma unroll
+                        for (int c = 0; c < OCW; ++c) tc::ld_16x32bx2_x16(tl + S::O_COL + oc0 + 32 * c, ov[c]);
+                        tc::ld_16x32bx2_x16(tl + S::L_COL, lv);
+                        tc::wait_ld();
+                        l = __shfl_sync(kFullMask, __uint_as_float(lv[0]), lane & 15);   // the L columns of half 0
+                    }
+                }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (!stop && lane == 0) mbar_arrive(smem_u32(o_free));
+            }
+            if (stop) {
+                if (lane == 0) fail_wait();
+                break;
+            }
+            if (!o_live) {
+                l = 0.f;
+#pragma unroll
+                for (int c = 0; c < OCW; ++c)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) ov[c][e] = 0u;
+            }
+            // (m, l, o) against the true maximum, as the warp-level kernel writes them
+            const float f = m_top == -INFINITY ? 0.f : ex2_ftz(m_ref - m_top);
+            l *= f;
+            const bool mine = hrow < nh;
+            const int64_t qhead = int64_t(g0.x) * a.Hq + int64_t(g0.y) * a.group + g0.z + hrow;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            if (sg.w < 0 && a.xworld) {
+                // the final row of this rank: to its slot in every rank's exchange buffer
+                for (int x = 0; x < a.xworld; ++x) {
+                    float *slot = xslot_of(a, x, xpar);
+                    if (mine) {
+                        store_o_part<OCW>(slot + qhead * D, ov, oc0, half, f * inv);
+                        if (cs == 0 && half == 0)
+                            *reinterpret_cast<float2 *>(xmeta_of<D>(slot, a, qhead)) = make_float2(m_top, l);
+                    }
+                }
+                // both warps' parts of these rows are stored: tag them
+                if (!pair_sync()) {
+                    if (lane == 0) fail_wait();
+                    stop = true;
+                    break;
+                }
+                if (cs == 0) publish_rows<D>(a, qhead - (lane & 15), max(0, min(16, nh - 16 * quad)), xpar, xe, lane);
+            } else {
+                // the group's only segment, seen whole by this CTA: final output;
+                // else the segment's (m, l, o) partial in slot sg.w
+                const int64_t pr = int64_t(sg.w) * GT + hrow;
+                if (mine) store_o_part<OCW>(sg.w < 0 ? a.out + qhead * D : a.part_o + pr * D, ov, oc0, half,
+                                            sg.w < 0 ? f * inv : f);
+                if (mine && cs == 0 && half == 0) {
+                    if (sg.w >= 0) a.part_ml[pr] = make_float2(m_top, l);
+                    else if (a.stats) reinterpret_cast<float2 *>(a.stats)[qhead] = make_float2(m_top, l);
+                }
+            }
+        }
+        tc::fence_before_sync();
+    }
+
+    // every tensor-memory access and MMA of this CTA is done: free the columns
+    named_barrier_sync(2, NC * 32);
+    if (warp == S::W_MMA) {
+        tc::fence_after_sync();
+        tc::dealloc(tmem, S::TMEM_COLS);
+    }
+    finish_decode<D, 1, GT, 1, NC, S::RING>(a, ring, flags, warp, lane, xpar, xe);
+    if (a.fused_merge || a.xworld) return;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace pd

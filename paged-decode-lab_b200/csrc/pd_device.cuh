@@ -60,10 +60,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// Non-blocking test of the same (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Wait for the phase with the given parity to complete; false after the timeout.
+// A phase that has completed already is seen by the non-blocking test.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           unsigned long long timeout_ns = kWaitTimeoutNs) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     const unsigned long long start = global_ns();
     for (;;) {
 #pragma unroll 1

@@ -6,6 +6,7 @@
 #pragma once
 
 #include "pd_decode_kernel.cuh"
+#include "pd_decode_mqa.cuh"
 #include "pd_kernels_select.hpp"
 
 namespace pd {
@@ -88,8 +89,18 @@ KernelEntry entry_for_hg(int hg) {
     }
 }
 
+// The tcgen05 kernel (decode only; the gather debug mode keeps the warp-level kernel).
+template <int D, int T>
+KernelEntry make_mqa_entry() {
+    using S = MqaShape<D, T>;
+    return {&paged_decode_mqa_kernel<D, T>, S::THREADS, S::SMEM, S::NC, S::SLOTS, 1};
+}
+
 template <typename Elt, int D, int T, int MODE>
-KernelEntry entry_for(int gt, int hg) {
+KernelEntry entry_for(int gt, int hg, int engine) {
+    if constexpr (MODE == kModeDecode && std::is_same<Elt, __half>::value) {
+        if (engine == kEngineTensorMemory && mqa_tensor_memory_shape(2, hg, gt, D, T)) return make_mqa_entry<D, T>();
+    }
     if (MODE == kModeGather || gt == 8) return entry_for_hg<Elt, D, T, 8, MODE>(hg);
     if (gt == 16) return entry_for_hg<Elt, D, T, 16, MODE>(hg);
     return entry_for_hg<Elt, D, T, 32, MODE>(hg);
@@ -105,21 +116,21 @@ cudaError_t launch_merge_shards(const float *shard_out, const float *shard_stats
                                 int64_t rows, int D, float *out, cudaStream_t stream);
 
 // Defined in the per-shape translation units.
-KernelEntry kernel_entry_f16_d64_t16(int gt, int hg, int mode);
-KernelEntry kernel_entry_f16_d64_t32(int gt, int hg, int mode);
-KernelEntry kernel_entry_f16_d128_t16(int gt, int hg, int mode);
-KernelEntry kernel_entry_f16_d128_t32(int gt, int hg, int mode);
-KernelEntry kernel_entry_f32_d64_t16(int gt, int hg, int mode);
-KernelEntry kernel_entry_f32_d64_t32(int gt, int hg, int mode);
-KernelEntry kernel_entry_f32_d128_t16(int gt, int hg, int mode);
-KernelEntry kernel_entry_f32_d128_t32(int gt, int hg, int mode);
+KernelEntry kernel_entry_f16_d64_t16(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f16_d64_t32(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f16_d128_t16(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f16_d128_t32(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f32_d64_t16(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f32_d64_t32(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f32_d128_t16(int gt, int hg, int mode, int engine);
+KernelEntry kernel_entry_f32_d128_t32(int gt, int hg, int mode, int engine);
 
 }  // namespace pd
 
-#define PD_DEFINE_ENTRY(NAME, ELT, D, T)                                        \
-    namespace pd {                                                             \
-    KernelEntry NAME(int gt, int hg, int mode) {                               \
-        return mode == kModeDecode ? entry_for<ELT, D, T, kModeDecode>(gt, hg) \
-                                   : entry_for<ELT, D, T, kModeGather>(gt, hg); \
-    }                                                                          \
+#define PD_DEFINE_ENTRY(NAME, ELT, D, T)                                                        \
+    namespace pd {                                                                             \
+    KernelEntry NAME(int gt, int hg, int mode, int engine) {                                   \
+        return mode == kModeDecode ? entry_for<ELT, D, T, kModeDecode>(gt, hg, engine)         \
+                                   : entry_for<ELT, D, T, kModeGather>(gt, hg, engine);        \
+    }                                                                                          \
     }

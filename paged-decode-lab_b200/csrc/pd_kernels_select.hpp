@@ -3,6 +3,17 @@
 
 namespace pd {
 
+// Consumer engines of the decode kernels: warp-level (m16n8k16 MMAs or FP32
+// FMAs in every consumer warp) or tcgen05 (one thread issues the MMAs into
+// tensor memory; pd_decode_mqa.cuh).
+enum : int { kEngineWarp = 0, kEngineTensorMemory = 1 };
+
+// Shapes the tcgen05 kernel serves: FP16 group tiles of 32 query heads (groups
+// of 17..32 query heads per KV head, MQA-like) over one KV head per page tile.
+inline constexpr bool mqa_tensor_memory_shape(int elt, int hg, int gt, int D, int T) {
+    return elt == 2 && hg == 1 && gt == 32 && (D == 64 || D == 128) && (T == 16 || T == 32);
+}
+
 // Consumer warps reading one page tile: HG KV heads x GT/8 query-head
 // slices each.  At most 8.
 inline constexpr int tile_consumers(int hg, int gt) { return hg * (gt / 8); }

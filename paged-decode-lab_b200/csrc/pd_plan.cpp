@@ -133,9 +133,18 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         const int kib = std::atoi(env);
         if (kib >= 1) target = kib * 1024;
     }
-    const int hg = choose_heads_per_tile(dtype == PD_FLOAT16 ? 2 : 4, L.head_dim, T, p.group_tile,
-                                         L.kv_heads, target);
+    // FP16 group tiles of 32 query heads run on the warp-level kernel
+    // (m16n8k16 MMAs, up to two KV heads per tile) unless PD_MQA_ENGINE=tcgen05
+    // selects the tcgen05 kernel (one KV head per page tile).
+    const char *engine_env = std::getenv("PD_MQA_ENGINE");
+    const bool tensor_memory = dtype == PD_FLOAT16 && p.group_tile == 32 && engine_env &&
+                               std::strcmp(engine_env, "tcgen05") == 0;
+    const int hg = tensor_memory ? 1
+                                 : choose_heads_per_tile(dtype == PD_FLOAT16 ? 2 : 4, L.head_dim, T, p.group_tile,
+                                                         L.kv_heads, target);
     p.heads_per_tile = hg;
+    p.engine = tensor_memory && mqa_tensor_memory_shape(2, hg, p.group_tile, L.head_dim, T) ? kEngineTensorMemory
+                                                                                          : kEngineWarp;
     const int kv_groups = L.kv_heads / hg;
     const int64_t ngroups = int64_t(L.batch) * kv_groups * p.group_splits;
     if (ngroups > INT32_MAX / 2) return fail(PD_ERR_VALUE, "too many (sequence, KV head) groups");
@@ -197,7 +206,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // final output itself.
     {
         const int elt = dtype == PD_FLOAT16 ? 2 : 4;
-        p.slot_stride = fold_sub_pipelines(elt, hg, p.group_tile, L.head_dim, T)
+        p.slot_stride = (p.engine == kEngineTensorMemory || fold_sub_pipelines(elt, hg, p.group_tile, L.head_dim, T))
                             ? 1
                             : max_sub_pipelines(elt, hg, p.group_tile, L.head_dim, T);
     }

@@ -46,6 +46,7 @@ struct pd_plan {
     int32_t group_tile = 8;        // GT: query heads processed together (8, 16, 32)
     int32_t group_splits = 1;      // ceil(G / GT)
     int32_t heads_per_tile = 1;    // HG: KV heads gathered per page tile
+    int32_t engine = 0;            // consumer engine of the decode kernel (kEngine*)
     int32_t num_ctas = 0;
     int32_t splits = 1;
     int32_t max_context = 0;

@@ -35,7 +35,8 @@ class PlanInfo(ctypes.Structure):
                 ("total_pages", ctypes.c_int32),
                 ("merge_rows", ctypes.c_int32), ("merge_in_kernel", ctypes.c_int32),
                 ("dynamic", ctypes.c_int32), ("max_span", ctypes.c_int32),
-                ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64)]
+                ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64),
+                ("engine", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 SIGNATURES = {
@@ -91,7 +92,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 6:
+        if lib.pd_abi_version() != 7:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

@@ -53,7 +53,11 @@ def check_worklist(layout, table, lengths, plan):
     # states inside the CTA (FP32, or four FP16 sub-pipelines), else one per sub-pipeline
     tile = 2 * layout.head_dim * 2 * T * hg
     nsub = 1 if tile >= 32768 else min(4, 8 // cpt)
-    assert stride == (1 if nsub >= 4 else max(1, nsub))
+    if info["engine"] == 1:
+        # FP16 group tiles of 32 query heads: the tcgen05 kernel, one KV head per tile
+        assert gt == 32 and hg == 1 and stride == 1
+    else:
+        assert stride == (1 if nsub >= 4 else max(1, nsub))
     covered = {gi: [] for gi in range(len(groups))}
     for c in range(C):
         for s in segs[offs[c]:offs[c + 1]]:

@@ -70,7 +70,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // of a page's rows for HG KV heads, landing in shared memory as
 // [head][128-byte box of the row][token] rows of 128 bytes, so the 128-byte
 // swizzle XORs by token and one instruction moves the whole K (or V) page.
-pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, int hg, CUtensorMap *map) {
+// With one_column the box is one 128-byte column of one head's page (T rows),
+// which the tcgen05 kernel places per column next to the step's other pages.
+pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, int hg, CUtensorMap *map,
+                           bool one_column = false) {
     auto encode = tensor_map_encoder();
     if (!encode) return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t elt = dtype == PD_FLOAT16 ? 2 : 4;
@@ -82,7 +85,8 @@ pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, i
     cuuint64_t dims[5] = {128 / elt, cuuint64_t(L.page_size), nbox, cuuint64_t(L.kv_heads),
                           cuuint64_t(L.physical_pages)};
     cuuint64_t strides[4] = {row * cuuint64_t(L.kv_heads), 128, row, row * cuuint64_t(L.kv_heads) * L.page_size};
-    cuuint32_t box[5] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(nbox), cuuint32_t(hg), 1};
+    cuuint32_t box[5] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(one_column ? 1 : nbox),
+                         cuuint32_t(hg), 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = encode(map,
                               dtype == PD_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -172,14 +176,16 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
         return fail(PD_ERR_VALUE, "k and v must be 16-byte aligned");
     TensorMapCache &tc = p->tmaps;
-    if (tc.k != k || tc.v != v || tc.dtype != int(dtype)) {
-        pd_status s = encode_cache_map(*p, k, dtype, p->heads_per_tile, &tc.map_k);
+    const int one_column = p->engine == kEngineTensorMemory && mode == kModeDecode ? 1 : 0;
+    if (tc.k != k || tc.v != v || tc.dtype != int(dtype) || tc.one_column != one_column) {
+        pd_status s = encode_cache_map(*p, k, dtype, p->heads_per_tile, &tc.map_k, one_column != 0);
         if (s != PD_OK) return s;
         s = encode_cache_map(*p, v, dtype, p->heads_per_tile, &tc.map_v);
         if (s != PD_OK) return s;
         tc.k = k;
         tc.v = v;
         tc.dtype = int(dtype);
+        tc.one_column = one_column;
     }
     const KernelEntry e =
         kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode,

@@ -6,18 +6,19 @@
 // src/paged_decode/csrc/decode.cu:26-168), with the consumer side rebuilt
 // around tcgen05:
 //
-//   * warp 7 (producer) streams page tiles (K then V of one page of one KV
-//     head) into the ring with TMA, as in the warp-level kernel;
+//   * warp 7 (producer) streams each page's K rows and V rows (one KV head)
+//     with TMA into two rings: K pages are free again once their scores are
+//     done, V pages once the step's PV products are;
 //   * warp 2 stages each segment's 32 query rows in shared memory (128-byte
 //     swizzled, K-major) two segments ahead;
-//   * one thread of warp 3 issues S = Q K^T for each page as it lands (M = 64
-//     rows of which the 32 query heads are 0..31, N = page tokens, K = head
-//     dim) into a double-buffered score block in tensor memory; one thread of
+//   * one thread of warp 3 issues S = Q K^T for a whole step once its K has
+//     landed (M = 64 rows of which the 32 query heads are 0..31, N = the
+//     step's NS tokens, K = head dim: one MMA per 16 head dims) into a
+//     double-buffered score block in tensor memory; one thread of
 //     warp 6, once a step's weights P are in shared memory, issues O += P V
-//     (N = head dim) and L += P 1 (the softmax denominators: the FP16 weights
-//     summed by the tensor core in FP32) into an output block in tensor
-//     memory.  Two issuing threads, so that neither kind waits for the other's
-//     inputs (pages landing, weights written);
+//     (N = head dim) into an output block in tensor memory.  Two issuing
+//     threads, so that neither kind waits for the other's inputs (K landing,
+//     weights written);
 //   * warps 0 and 4 own query heads 0..15, warps 1 and 5 heads 16..31
 //     (tensor-memory lanes 0..15 of sub-partitions 0 and 1); of each step's
 //     NS score columns a warp takes one half, two threads per head.  Online
@@ -30,11 +31,11 @@
 //     partial, m the true maximum).
 //
 // A step is NP consecutive pages of one segment (NS = NP * T score columns).
-// mbarriers order the roles: ring full/empty (TMA -> MMA), q_full/q_empty
-// (query rows), s_full (scores ready), p_full (weights written), p_free (the
-// step's PV products done: its weights and ring slots are free, the output
-// block quiescent), o_free (a segment's output read back), pair (the two
-// softmax warps of the same heads).  Every wait is bounded; on a timeout the
+// mbarriers order the roles: K and V ring full/empty (TMA -> score / PV
+// MMAs), q_full/q_empty (query rows), s_full (scores ready), p_full (weights
+// written), p_free (the step's PV products done: its weights and V pages are
+// free, the output block quiescent), o_free (a segment's output read back),
+// pair (the two softmax warps of the same heads).  Every wait is bounded; on a timeout the
 // CTA records PD_DEVERR_TIMEOUT, unwinds, waits for its own MMAs and frees its
 // tensor memory.
 #pragma once
@@ -56,7 +57,6 @@ struct MqaShape {
     static constexpr int ROW_BYTES = D * 2;
     static constexpr int NBOX = ROW_BYTES / 128;        // 128-byte boxes per token row
     static constexpr int HALF_BYTES = NBOX * T * 128;   // K (or V) rows of one page: [box][token]
-    static constexpr int TILE_BYTES = 2 * HALF_BYTES;
     static constexpr int NS = 128;                      // score columns per step
     static constexpr int NP = NS / T;                   // pages per step
     static constexpr int KSTEPS = D / 16;               // K = 16 MMAs of S = Q K^T
@@ -67,7 +67,6 @@ struct MqaShape {
     static constexpr int Q_BYTES = NBOX * Q_BOX;
     static constexpr int P_SBO = NS * 16;               // 8 rows of NS FP16 weights (8x8 core matrices)
     static constexpr int P_BYTES = (GT / 8) * P_SBO;
-    static constexpr int ONES_BYTES = 512;              // B = 1 (16 tokens x 16 columns) for L += P 1
     // An M = 64 MMA reads 64 rows of A; rows 32..63 (never read back from
     // tensor memory) come from whatever follows the 32 written rows, which
     // must be allocated shared memory: P buffer 1 reads on into the Q
@@ -75,29 +74,37 @@ struct MqaShape {
     static constexpr int P_READ = (M / 8) * P_SBO;                      // from a P buffer's start
     static constexpr int Q_READ = (NBOX - 1) * Q_BOX + (M / 8) * 1024;  // from a Q buffer's start
     static constexpr int GUARD = Q_READ > Q_BYTES ? Q_READ - Q_BYTES : 0;
-    // tensor-memory columns: O block [0, D), L block [D, D + 32) (16 written),
-    // score blocks [S_COL, S_COL + NS), [S_COL + NS, S_COL + 2 NS)
+    // tensor-memory columns: O block [0, D), score blocks [D, D + NS), [D + NS, D + 2 NS)
     static constexpr int O_COL = 0;
-    static constexpr int L_COL = D;
-    static constexpr int S_COL = D + 32;
+    static constexpr int S_COL = D;
     static constexpr int TMEM_COLS = (S_COL + 2 * NS) <= 256 ? 256 : 512;
     static constexpr int NBARS = 18;   // s_full, p_full, p_free, q_full, q_empty: 2 each; pair: 4; o_free; mma_done: 2
-    static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] floats
-    static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + GUARD + ONES_BYTES +
-                                    NBARS * 8 + XMAX_BYTES + 16 + 16 + 16;
-    static constexpr int FIT = int((232448 - FIXED) / (TILE_BYTES + 8 + 8 + 4));
-    static constexpr int SLOTS = FIT > 32 ? 32 : FIT;
-    static constexpr size_t RING = size_t(SLOTS) * TILE_BYTES;
-    static constexpr size_t SMEM = FIXED + RING + size_t(SLOTS) * 20;
+    static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] row maxima
+    static constexpr int XL_BYTES = 2 * 2 * 16 * 4;         // [heads half][warp][row] denominators
+    // K arrives a step at a time into KSS step slots laid out [box][NS tokens]
+    // [128 B], so one MMA takes a whole step's scores per 16 head dims; a step
+    // slot is free once those scores are done.  V arrives a page at a time
+    // into VS page slots and is free once its step's PV products are; the V
+    // ring holds two steps and streams ahead with the rest.  Per slot: full and
+    // empty mbarriers and a valid word (20 bytes).
+    static constexpr int KSTEP_BYTES = NBOX * NS * 128;
+    static constexpr int KSS = 2;
+    static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + GUARD + NBARS * 8 +
+                                    XMAX_BYTES + XL_BYTES + 16 + 16 + 16 + size_t(KSS) * (KSTEP_BYTES + 20);
+    static constexpr int VFIT = int((232448 - FIXED) / (HALF_BYTES + 20));
+    static constexpr int VS = VFIT > 48 ? 48 : VFIT;
+    static constexpr size_t RING = size_t(KSS) * KSTEP_BYTES + size_t(VS) * HALF_BYTES;   // [K steps][V pages]
+    static constexpr size_t SMEM = FIXED + size_t(VS) * (HALF_BYTES + 20);
 
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
     static_assert(T == 16 || T == 32, "page_size 16 or 32");
     static_assert(NS == 64 || NS == 128, "a step is 64 or 128 score columns");
     static_assert(P_READ <= P_BYTES + 2 * Q_BYTES, "P buffer 1's unread rows must stay inside the Q buffers");
     static_assert(S_COL + 2 * NS <= TMEM_COLS, "tensor memory budget");
-    // a step's slots are released after its PV products: the ring must hold
-    // two steps at once, and then some to stream ahead
-    static_assert(SLOTS >= 2 * NP + 2, "ring too small for two steps in flight");
+    static_assert(NP * (T * 128) % 1024 == 0 && (T * 128) % 1024 == 0, "pages keep 1024-byte swizzle atoms");
+    // a step's V pages are released after its PV products: the V ring must
+    // hold two steps at once, and then some to stream ahead
+    static_assert(VS >= 2 * NP + 2, "V ring too small for the steps in flight");
     static_assert(SMEM <= 232448 && SMEM > 116 * 1024,
                   "one CTA per SM: its tensor memory is never contended by a second CTA of the grid");
 };
@@ -130,22 +137,120 @@ __device__ __forceinline__ float ex2_ftz(float x) {
     return r;
 }
 
+// Producer warp of the tcgen05 kernel: two lanes, each walking the CTA's work
+// list on its own, so that neither kind of load waits for the other's slots.
+//   lane 0, K by steps (NP consecutive pages of one segment): step s into step
+//     slot s % KSS, one TMA load per page and 128-byte column (page p, column b
+//     at b * NS * 128 + p * T * 128), once the scores of step s - KSS are done;
+//   lane 1, V by pages: page j's rows into V slot j % VS (one load,
+//     [column][token]) once the PV products of page j - VS are done.
+// Pages past a dynamic plan's live length, or with an id outside the cache,
+// land nothing and are marked invalid (K: a bit per page of the step; V: per
+// slot).  Waits poll without suspending: the two lanes share one warp.
+template <int T, int NP, int NS, int NBOX, int HALF_BYTES, int KSTEP_BYTES, int KSS, int VS>
+__device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const CUtensorMap *tm_v,
+                                                 const DecodeArgs &a, uint8_t *kring, uint8_t *vring,
+                                                 uint64_t *kfull, uint64_t *kempty, uint64_t *vfull,
+                                                 uint64_t *vempty, unsigned *kvalid, int *vvalid,
+                                                 SmemFlags *flags, int seg_begin, int seg_end, int lane) {
+    if (lane > 1) return;
+    tma_prefetch_descriptor(lane == 0 ? tm_k : tm_v);
+    const auto claim = [&](uint64_t *empty, int use) -> bool {
+        if (use == 0) return !flags->abort;
+        const uint32_t bar = smem_u32(empty), par = (use - 1) & 1;
+        const unsigned long long t0 = global_ns();
+        while (!mbar_test_wait(bar, par)) {
+            if (flags->abort) return false;
+            if (global_ns() - t0 > kWaitTimeoutNs) {
+                atomicOr(a.error, kErrTimeout);
+                flags->abort = 1;
+                return false;
+            }
+        }
+        return true;
+    };
+    // 0: stream it; 1: not live yet; 2: id outside the cache (the reference
+    // skips those tokens, decode.cu:58; plans validate ids, so this is defence only)
+    const auto page_state = [&](int id, int64_t first_token, int live_end) {
+        return first_token >= live_end ? 1 : (id >= 0 && int64_t(id) < a.P) ? 0 : 2;
+    };
+    int gs = 0, j = 0;
+    for (int si = seg_begin; si < seg_end; ++si) {
+        const int4 sg = __ldg(a.segs + si);
+        const int npg = sg.z - sg.y;
+        if (npg == 0) continue;
+        const int4 g0 = __ldg(a.groups + 2 * sg.x);
+        const int32_t *trow = a.table + int64_t(g0.x) * a.W + sg.y;
+        const int live_end = a.dynamic ? max(0, a.lengths[g0.x]) : INT_MAX;
+        for (int p0 = 0; p0 < npg; p0 += NP) {
+            const int n = min(NP, npg - p0);
+            if (lane == 0) {
+                const int ks = gs % KSS;
+                int ids[NP];
+                unsigned mask = 0;
+#pragma unroll
+                for (int p = 0; p < NP; ++p) {
+                    ids[p] = p < n ? __ldg(trow + p0 + p) : 0;
+                    const int st = p < n ? page_state(ids[p], int64_t(sg.y + p0 + p) * T, live_end) : 1;
+                    if (st == 2) atomicOr(a.error, kErrBadPage);
+                    if (st == 0) mask |= 1u << p;
+                }
+                if (!claim(kempty + ks, gs / KSS)) return;
+                const uint32_t fb = smem_u32(kfull + ks);
+                kvalid[ks] = mask;
+                if (mask) mbar_arrive_expect_tx(fb, uint32_t(__popc(mask)) * HALF_BYTES);
+                else mbar_arrive(fb);
+#pragma unroll
+                for (int p = 0; p < NP; ++p)
+                    if ((mask >> p) & 1u) {
+#pragma unroll
+                        for (int b = 0; b < NBOX; ++b)
+                            tma_load_5d(smem_u32(kring + size_t(ks) * KSTEP_BYTES + b * (NS * 128) + p * (T * 128)),
+                                        tm_k, 0, 0, b, g0.y, ids[p], fb);
+                    }
+            } else {
+                for (int p = 0; p < n; ++p) {
+                    const int jj = j + p, slot = jj % VS;
+                    const int id = __ldg(trow + p0 + p);
+                    const int st = page_state(id, int64_t(sg.y + p0 + p) * T, live_end);
+                    if (!claim(vempty + slot, jj / VS)) return;
+                    const uint32_t fb = smem_u32(vfull + slot);
+                    if (st != 0) {
+                        vvalid[slot] = 0;
+                        mbar_arrive(fb);
+                    } else {
+                        vvalid[slot] = 1;
+                        mbar_arrive_expect_tx(fb, HALF_BYTES);
+                        tma_load_5d(smem_u32(vring + size_t(slot) * HALF_BYTES), tm_v, 0, 0, 0, g0.y, id, fb);
+                    }
+                }
+            }
+            ++gs;
+            j += n;
+        }
+    }
+}
+
 template <int D, int T>
 __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     paged_decode_mqa_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const DecodeArgs a) {
     using S = MqaShape<D, T>;
-    constexpr int NC = S::NC, NS = S::NS, NP = S::NP, SLOTS = S::SLOTS, GT = S::GT, OCW = S::OCW, CW = S::CW;
+    constexpr int NC = S::NC, NS = S::NS, NP = S::NP, KSS = S::KSS, VS = S::VS, GT = S::GT, OCW = S::OCW,
+                  CW = S::CW, HALF = S::HALF_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
+    uint8_t *kring = ring;                                  // [KSS][box][NS tokens][128 B]
+    uint8_t *vring = ring + size_t(KSS) * S::KSTEP_BYTES;   // [VS][box][T tokens][128 B]
     uint8_t *pbuf = ring + S::RING;
     uint8_t *qbuf = pbuf + 2 * S::P_BYTES;
-    uint8_t *ones = qbuf + 2 * S::Q_BYTES + S::GUARD;
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(ones + S::ONES_BYTES);
-    uint64_t *empty_bar = full_bar + SLOTS;
-    uint64_t *s_full = empty_bar + SLOTS;   // [2] per score block
+    uint64_t *kfull = reinterpret_cast<uint64_t *>(qbuf + 2 * S::Q_BYTES + S::GUARD);
+    uint64_t *kempty = kfull + KSS;
+    uint64_t *vfull = kempty + KSS;
+    uint64_t *vempty = vfull + VS;
+    uint64_t *s_full = vempty + VS;         // [2] per score block
     uint64_t *p_full = s_full + 2;          // [2] per weight buffer
     uint64_t *p_free = p_full + 2;          // [2]
     uint64_t *q_full = p_free + 2;          // [2] per query buffer
@@ -154,9 +259,11 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     uint64_t *o_free = pair_bar + 4;
     uint64_t *mma_done = o_free + 1;        // [2] score MMAs, PV MMAs
     float *xmax = reinterpret_cast<float *>(mma_done + 2);
-    unsigned *svalid = reinterpret_cast<unsigned *>(xmax + S::XMAX_BYTES / 4);   // [2]: pages streamed, per score block
-    int *slot_valid = reinterpret_cast<int *>(svalid + 4);
-    SmemFlags *flags = reinterpret_cast<SmemFlags *>(slot_valid + SLOTS);
+    float *xl = xmax + S::XMAX_BYTES / 4;
+    unsigned *svalid = reinterpret_cast<unsigned *>(xl + S::XL_BYTES / 4);   // [2]: pages streamed, per score block
+    unsigned *kvalid = svalid + 4;                                           // [KSS]: pages streamed, per K step
+    int *vvalid = reinterpret_cast<int *>(kvalid + KSS);
+    SmemFlags *flags = reinterpret_cast<SmemFlags *>(vvalid + VS);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(flags + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -166,9 +273,13 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     const int seg_end = __shfl_sync(kFullMask, hv.y, 0);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SLOTS; ++s) {
-            mbar_init(smem_u32(full_bar + s), 1);
-            mbar_init(smem_u32(empty_bar + s), 1);   // one commit of the MMA thread
+        for (int s = 0; s < KSS; ++s) {
+            mbar_init(smem_u32(kfull + s), 1);
+            mbar_init(smem_u32(kempty + s), 1);   // one commit of the score thread
+        }
+        for (int s = 0; s < VS; ++s) {
+            mbar_init(smem_u32(vfull + s), 1);
+            mbar_init(smem_u32(vempty + s), 1);   // one commit of the PV thread
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(s_full + b), 2);      // the scores' commit and the MMA thread (svalid)
@@ -200,8 +311,9 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     const int xpar = int(xe & 1u);
 
     if (warp == NC) {
-        stream_page_tiles<T, S::TILE_BYTES, S::HALF_BYTES, SLOTS>(&tm_k, &tm_v, a, ring, full_bar, empty_bar,
-                                                                slot_valid, flags, hv, seg_begin, seg_end, lane);
+        stream_mqa_pages<T, NP, NS, S::NBOX, HALF, S::KSTEP_BYTES, KSS, VS>(
+            &tm_k, &tm_v, a, kring, vring, kfull, kempty, vfull, vempty, kvalid, vvalid, flags, seg_begin, seg_end,
+            lane);
         return;
     }
 
@@ -219,9 +331,6 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
 
     if (warp == S::W_Q) {
         // ------------------------------------------------------------ query rows
-        // B = 1 for L += P 1, once: 16 x 16 FP16 ones in 8x8 core matrices.
-        for (int e = lane; e < S::ONES_BYTES / 16; e += 32)
-            reinterpret_cast<uint4 *>(ones)[e] = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
         // Segment sc (counting segments with pages) goes to buffer sc % 2 once
         // the score MMAs of segment sc - 2 are done: row g of the tile at
         // [box][row][128 B], 16-byte chunks XORed by row % 8 (the layout the
@@ -255,10 +364,11 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         }
     } else if (warp == S::W_MMA) {
         // ------------------------------------------------------------ score MMAs (one thread)
-        // S = Q K^T for each page as it lands, into score block gs % 2 once the
+        // S = Q K^T for a step once its K has landed (one MMA per 16 head dims
+        // over all NS tokens of the step), into score block gs % 2 once the
         // weights of step gs - 2 (which read that block) are written.
         if (lane == 0) {
-            constexpr uint32_t ID_S = tc::idesc_f16_f32(S::M, T, false, false);   // Q, K: K-major
+            constexpr uint32_t ID_S = tc::idesc_f16_f32(S::M, NS, false, false);   // Q, K: K-major
             bool stop = false;
             int gs = 0, j = 0, sc = 0;
             for (int si = seg_begin; si < seg_end && !stop; ++si) {
@@ -278,27 +388,27 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         stop = true;
                         break;
                     }
+                    const int ks = gs % KSS;
+                    if (!mbar_wait(smem_u32(kfull + ks), (gs / KSS) & 1)) {
+                        stop = true;
+                        break;
+                    }
                     tc::fence_after_sync();
-                    unsigned valid = 0;
-                    for (int p = 0; p < n; ++p) {
-                        const int jj = j + p;
-                        const int slot = jj % SLOTS;
-                        if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {
-                            stop = true;
-                            break;
-                        }
-                        if (!slot_valid[slot]) continue;
-                        valid |= 1u << p;
-                        const uint32_t kb = smem_u32(ring + size_t(slot) * S::TILE_BYTES);
+                    // pages past the step's n, or not streamed, leave stale rows: their
+                    // score columns are masked by the softmax
+                    const unsigned valid = kvalid[ks] & ((1u << n) - 1u);
+                    if (valid) {
+                        const uint32_t kb = smem_u32(kring + size_t(ks) * S::KSTEP_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < S::KSTEPS; ++kk) {
-                            const uint32_t koff = (kk >> 2) * (T * 128) + (kk & 3) * 32;
+                            const uint32_t koff = (kk >> 2) * (NS * 128) + (kk & 3) * 32;
                             const uint64_t ad = tc::smem_desc(qa + (kk >> 2) * S::Q_BOX + (kk & 3) * 32, 16, 1024,
                                                               tc::kSwizzle128);
                             const uint64_t bd = tc::smem_desc(kb + koff, 16, 1024, tc::kSwizzle128);
-                            tc::mma_f16(tmem + S::S_COL + b * NS + p * T, ad, bd, ID_S, kk > 0 ? 1u : 0u);
+                            tc::mma_f16(tmem + S::S_COL + b * NS, ad, bd, ID_S, kk > 0 ? 1u : 0u);
                         }
                     }
+                    tc::commit(smem_u32(kempty + ks));   // the step's K, once these scores are done
                     if (stop) break;
                     tc::commit(smem_u32(s_full + b));
                     svalid[b] = valid;
@@ -317,14 +427,12 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         __syncwarp();
     } else if (warp == S::W_PV) {
         // ------------------------------------------------------------ PV MMAs (one thread)
-        // Once a step's weights are written: O += P V and L += P 1 (a segment's
-        // first product overwrites, after the previous segment's output block
-        // was read back), then commits that free the weight buffer and the
-        // step's ring slots.
+        // Once a step's weights are written: O += P V for each page as its V
+        // lands (a segment's first product overwrites, after the previous
+        // segment's output block was read back), then commits that free the
+        // weight buffer and the step's V pages.
         if (lane == 0) {
             constexpr uint32_t ID_O = tc::idesc_f16_f32(S::M, D, false, true);    // P K-major, V MN-major
-            constexpr uint32_t ID_L = tc::idesc_f16_f32(S::M, 16, false, false);  // P, ones: K-major
-            const uint64_t ones_desc = tc::smem_desc(smem_u32(ones), 128, 256, tc::kNoSwizzle);
             bool stop = false;
             int gs = 0, j = 0, sc = 0;
             for (int si = seg_begin; si < seg_end && !stop; ++si) {
@@ -344,26 +452,25 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                     const uint32_t pb = smem_u32(pbuf + b * S::P_BYTES);
                     for (int p = 0; p < n; ++p) {
                         const int jj = j + p;
-                        const int slot = jj % SLOTS;
-                        if (!mbar_wait(smem_u32(full_bar + slot), (jj / SLOTS) & 1)) {   // seen already
+                        const int slot = jj % VS;
+                        if (!mbar_wait(smem_u32(vfull + slot), (jj / VS) & 1)) {
                             stop = true;
                             break;
                         }
-                        if (!slot_valid[slot]) continue;
-                        const uint32_t vb = smem_u32(ring + size_t(slot) * S::TILE_BYTES) + S::HALF_BYTES;
+                        if (!vvalid[slot]) continue;
+                        const uint32_t vb = smem_u32(vring + size_t(slot) * HALF);
 #pragma unroll
                         for (int kk = 0; kk < S::PSTEPS; ++kk) {
                             const uint64_t ad =
                                 tc::smem_desc(pb + (p * S::PSTEPS + kk) * 256, 128, S::P_SBO, tc::kNoSwizzle);
                             const uint64_t bd = tc::smem_desc(vb + kk * 16 * 128, T * 128, 1024, tc::kSwizzle128);
                             tc::mma_f16(tmem + S::O_COL, ad, bd, ID_O, accumulate);
-                            tc::mma_f16(tmem + S::L_COL, ad, ones_desc, ID_L, accumulate);
                             accumulate = 1;
                         }
                     }
                     if (stop) break;
                     tc::commit(smem_u32(p_free + b));
-                    for (int p = 0; p < n; ++p) tc::commit(smem_u32(empty_bar + (j + p) % SLOTS));
+                    for (int p = 0; p < n; ++p) tc::commit(smem_u32(vempty + (j + p) % VS));
                     ++gs;
                     j += n;
                 }
@@ -472,19 +579,28 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                     }
                     // row hrow, tokens c0 + 32c + 16 half + [0, 16): two 8x8 core matrices
                     const uint32_t prow = smem_u32(pbuf + b * S::P_BYTES) + (hrow & 7) * 16 + (hrow >> 3) * S::P_SBO;
+                    float lstep = 0.f;
 #pragma unroll
                     for (int c = 0; c < CW; ++c) {
+                        float pw[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) pw[e] = ex2_ftz(fmaf(__uint_as_float(sv[c][e]), a.scale_log2, nu));
                         uint32_t w[8];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            w[e] = pack_half2(ex2_ftz(fmaf(__uint_as_float(sv[c][2 * e]), a.scale_log2, nu)),
-                                              ex2_ftz(fmaf(__uint_as_float(sv[c][2 * e + 1]), a.scale_log2, nu)));
+                        for (int e = 0; e < 8; ++e) w[e] = pack_half2(pw[2 * e], pw[2 * e + 1]);
+                        // this thread's share of the denominator, summed as a tree
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) pw[e] = pw[2 * e] + pw[2 * e + 1];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) pw[e] = pw[2 * e] + pw[2 * e + 1];
+                        lstep += (pw[0] + pw[1]) + (pw[2] + pw[3]);
                         const uint32_t at = prow + ((c0 + 32 * c + 16 * half) >> 3) * 128;
                         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(at), "r"(w[0]), "r"(w[1]),
                                      "r"(w[2]), "r"(w[3]) : "memory");
                         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(at + 128), "r"(w[4]),
                                      "r"(w[5]), "r"(w[6]), "r"(w[7]) : "memory");
                     }
+                    l = fmaf(l, alpha, lstep);
                     // V rows past the sequence end in its last page may hold anything,
                     // NaN included; their weight 0 must not meet them in the MMA.
                     if (quad == 0) {
@@ -492,11 +608,11 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         const int vt = (length - tok0) - pz * T;
                         if (length > tok0 && pz < n && vt > 0 && ((valid >> pz) & 1u)) {
                             // the page's load landed (seen here too, before writing over it)
-                            if (!warp_wait(full_bar + (j + pz) % SLOTS, ((j + pz) / SLOTS) & 1)) {
+                            if (!warp_wait(vfull + (j + pz) % VS, ((j + pz) / VS) & 1)) {
                                 stop = true;
                                 break;
                             }
-                            uint8_t *vrows = ring + size_t((j + pz) % SLOTS) * S::TILE_BYTES + S::HALF_BYTES;
+                            uint8_t *vrows = vring + size_t((j + pz) % VS) * HALF;
                             constexpr int UPR = S::NBOX * 8;   // 16-byte units per token row
                             for (int e = cs * 32 + lane; e < (T - vt) * UPR; e += 64) {
                                 const int row = vt + e / UPR, u16 = e % UPR;
@@ -507,7 +623,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                     }
                     // A moved reference rescales what the earlier steps built: the two
                     // warps of these heads see the same maxima, so both take this branch
-                    // (each its part of the output block, warp cs = 1 also the L block).
+                    // (each its part of the output block).
                     if (__any_sync(kFullMask, grow && o_live)) {
                         if (!warp_wait(p_free + ((gs - 1) & 1), ((gs - 1) >> 1) & 1)) {
                             stop = true;
@@ -515,9 +631,8 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         }
                         tc::fence_after_sync();
 #pragma unroll
-                        for (int c = 0; c <= OCW; ++c) {
-                            if (c == OCW && cs == 0) break;
-                            const uint32_t col = c < OCW ? S::O_COL + oc0 + 32 * c : S::L_COL;
+                        for (int c = 0; c < OCW; ++c) {
+                            const uint32_t col = S::O_COL + oc0 + 32 * c;
                             uint32_t r[16];
                             tc::ld_16x32bx2_x16(tl + col, r);
                             tc::wait_ld();
@@ -541,12 +656,9 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         stop = true;
                     } else {
                         tc::fence_after_sync();
-                        uint32_t lv[16];
 #pragma unroll
                         for (int c = 0; c < OCW; ++c) tc::ld_16x32bx2_x16(tl + S::O_COL + oc0 + 32 * c, ov[c]);
-                        tc::ld_16x32bx2_x16(tl + S::L_COL, lv);
                         tc::wait_ld();
-                        l = __shfl_sync(kFullMask, __uint_as_float(lv[0]), lane & 15);   // the L columns of half 0
                     }
                 }
                 tc::fence_before_sync();
@@ -563,6 +675,18 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                 for (int c = 0; c < OCW; ++c)
 #pragma unroll
                     for (int e = 0; e < 16; ++e) ov[c][e] = 0u;
+            } else {
+                // the row's denominator: this warp's two halves, then both warps, added
+                // in warp order so that both hold the same bits
+                const float lw = l + __shfl_xor_sync(kFullMask, l, 16);
+                float *xr = xl + quad * 32;
+                if (half == 0) xr[cs * 16 + (lane & 15)] = lw;
+                if (!pair_sync()) {
+                    if (lane == 0) fail_wait();
+                    stop = true;
+                    break;
+                }
+                l = xr[lane & 15] + xr[16 + (lane & 15)];
             }
             // (m, l, o) against the true maximum, as the warp-level kernel writes them
             const float f = m_top == -INFINITY ? 0.f : ex2_ftz(m_ref - m_top);

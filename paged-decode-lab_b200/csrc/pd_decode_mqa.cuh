@@ -74,11 +74,11 @@ struct MqaShape {
     static constexpr int P_READ = (M / 8) * P_SBO;                      // from a P buffer's start
     static constexpr int Q_READ = (NBOX - 1) * Q_BOX + (M / 8) * 1024;  // from a Q buffer's start
     static constexpr int GUARD = Q_READ > Q_BYTES ? Q_READ - Q_BYTES : 0;
-    // tensor-memory columns: O block [0, D), score blocks [D, D + NS), [D + NS, D + 2 NS)
-    static constexpr int O_COL = 0;
-    static constexpr int S_COL = D;
+    // tensor-memory columns: output blocks [0, D) and [D, 2 D) (alternate segments),
+    // score blocks [2 D, 2 D + NS), [2 D + NS, 2 D + 2 NS)
+    static constexpr int S_COL = 2 * D;
     static constexpr int TMEM_COLS = (S_COL + 2 * NS) <= 256 ? 256 : 512;
-    static constexpr int NBARS = 18;   // s_full, p_full, p_free, q_full, q_empty: 2 each; pair: 4; o_free; mma_done: 2
+    static constexpr int NBARS = 20;   // s_full, p_full, p_free, q_full, q_empty, o_free, mma_done: 2 each; pair: 4
     static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] row maxima
     static constexpr int XL_BYTES = 2 * 2 * 16 * 4;         // [heads half][warp][row] denominators
     // K arrives a step at a time into KSS step slots laid out [box][NS tokens]
@@ -256,8 +256,8 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     uint64_t *q_full = p_free + 2;          // [2] per query buffer
     uint64_t *q_empty = q_full + 2;         // [2]
     uint64_t *pair_bar = q_empty + 2;       // [2 heads halves][2 phases]
-    uint64_t *o_free = pair_bar + 4;
-    uint64_t *mma_done = o_free + 1;        // [2] score MMAs, PV MMAs
+    uint64_t *o_free = pair_bar + 4;        // [2] per output block
+    uint64_t *mma_done = o_free + 2;        // [2] score MMAs, PV MMAs
     float *xmax = reinterpret_cast<float *>(mma_done + 2);
     float *xl = xmax + S::XMAX_BYTES / 4;
     unsigned *svalid = reinterpret_cast<unsigned *>(xl + S::XL_BYTES / 4);   // [2]: pages streamed, per score block
@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         }
         for (int i = 0; i < 4; ++i) mbar_init(smem_u32(pair_bar + i), 2);
         mbar_init(smem_u32(o_free), 4);
+        mbar_init(smem_u32(o_free + 1), 4);
         mbar_init(smem_u32(mma_done), 1);
         mbar_init(smem_u32(mma_done + 1), 1);
         flags->abort = 0;
@@ -443,8 +444,9 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                 for (int p0 = 0; p0 < npg; p0 += NP) {
                     const int n = min(NP, npg - p0);
                     const int b = gs & 1;
+                    // output block sc % 2 was read back for segment sc - 2
                     if (!mbar_wait(smem_u32(p_full + b), (gs >> 1) & 1) ||
-                        (p0 == 0 && sc > 0 && !mbar_wait(smem_u32(o_free), (sc - 1) & 1))) {
+                        (p0 == 0 && sc >= 2 && !mbar_wait(smem_u32(o_free + (sc & 1)), ((sc >> 1) - 1) & 1))) {
                         stop = true;
                         break;
                     }
@@ -464,7 +466,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                             const uint64_t ad =
                                 tc::smem_desc(pb + (p * S::PSTEPS + kk) * 256, 128, S::P_SBO, tc::kNoSwizzle);
                             const uint64_t bd = tc::smem_desc(vb + kk * 16 * 128, T * 128, 1024, tc::kSwizzle128);
-                            tc::mma_f16(tmem + S::O_COL, ad, bd, ID_O, accumulate);
+                            tc::mma_f16(tmem + (sc & 1) * D, ad, bd, ID_O, accumulate);
                             accumulate = 1;
                         }
                     }
@@ -501,6 +503,83 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
             ++npair;
             return ok;
         };
+        // A segment's output is read back and written once the next segment's
+        // first weights are out (or after the last segment), so the softmax does
+        // not wait for the segment's last PV products; the output blocks of
+        // consecutive segments alternate (sc % 2).
+        struct Seg {
+            int4 sg, g0;
+            int nh, last_gs, ob;
+            float m_ref, m_top, l;   // l: this thread's share of the denominator
+            bool o_live;             // a PV product was issued into output block ob
+            bool tmem;               // the segment had pages (its output block is released)
+        };
+        const auto finish = [&](const Seg &q) -> bool {
+            uint32_t ov[OCW][16];    // this warp's part of the output row
+            float l = q.l;
+            if (q.o_live) {
+                if (!warp_wait(p_free + (q.last_gs & 1), (q.last_gs >> 1) & 1)) return false;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int c = 0; c < OCW; ++c) tc::ld_16x32bx2_x16(tl + q.ob * D + oc0 + 32 * c, ov[c]);
+                tc::wait_ld();
+            }
+            if (q.tmem) {
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(o_free + q.ob));
+            }
+            if (!q.o_live) {
+                l = 0.f;
+#pragma unroll
+                for (int c = 0; c < OCW; ++c)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) ov[c][e] = 0u;
+            } else {
+                // the row's denominator: this warp's two halves, then both warps, added
+                // in warp order so that both hold the same bits
+                const float lw = l + __shfl_xor_sync(kFullMask, l, 16);
+                float *xr = xl + quad * 32;
+                if (half == 0) xr[cs * 16 + (lane & 15)] = lw;
+                if (!pair_sync()) return false;
+                l = xr[lane & 15] + xr[16 + (lane & 15)];
+            }
+            // (m, l, o) against the true maximum, as the warp-level kernel writes them
+            const float f = q.m_top == -INFINITY ? 0.f : ex2_ftz(q.m_ref - q.m_top);
+            l *= f;
+            const bool mine = hrow < q.nh;
+            const int64_t qhead = int64_t(q.g0.x) * a.Hq + int64_t(q.g0.y) * a.group + q.g0.z + hrow;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            if (q.sg.w < 0 && a.xworld) {
+                // the final row of this rank: to its slot in every rank's exchange buffer
+                for (int x = 0; x < a.xworld; ++x) {
+                    float *slot = xslot_of(a, x, xpar);
+                    if (mine) {
+                        store_o_part<OCW>(slot + qhead * D, ov, oc0, half, f * inv);
+                        if (cs == 0 && half == 0)
+                            *reinterpret_cast<float2 *>(xmeta_of<D>(slot, a, qhead)) = make_float2(q.m_top, l);
+                    }
+                }
+                // both warps' parts of these rows are stored: tag them
+                if (!pair_sync()) return false;
+                if (cs == 0)
+                    publish_rows<D>(a, qhead - (lane & 15), max(0, min(16, q.nh - 16 * quad)), xpar, xe, lane);
+            } else {
+                // the group's only segment, seen whole by this CTA: final output;
+                // else the segment's (m, l, o) partial in slot sg.w
+                const int64_t pr = int64_t(q.sg.w) * GT + hrow;
+                if (mine) store_o_part<OCW>(q.sg.w < 0 ? a.out + qhead * D : a.part_o + pr * D, ov, oc0, half,
+                                            q.sg.w < 0 ? f * inv : f);
+                if (mine && cs == 0 && half == 0) {
+                    if (q.sg.w >= 0) a.part_ml[pr] = make_float2(q.m_top, l);
+                    else if (a.stats) reinterpret_cast<float2 *>(a.stats)[qhead] = make_float2(q.m_top, l);
+                }
+            }
+            return true;
+        };
+        Seg pend{};
+        bool has_pend = false;
+        int sc = 0;   // segments with pages so far: this one's output block is sc % 2
         int gs = 0, j = 0;
         bool stop = false;
         for (int si = seg_begin; si < seg_end; ++si) {
@@ -518,7 +597,6 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
             float m_ref = -INFINITY;   // the maximum the weights are taken against
             float m_top = -INFINITY;   // the true running maximum
             bool o_live = false;       // a PV product has been issued in this segment
-            uint32_t ov[OCW][16];      // this warp's part of the output row at the segment end
             float l = 0.f;
             if (npg > 0 && !stop) {
                 for (int p0 = 0; p0 < npg; p0 += NP) {
@@ -632,7 +710,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         tc::fence_after_sync();
 #pragma unroll
                         for (int c = 0; c < OCW; ++c) {
-                            const uint32_t col = S::O_COL + oc0 + 32 * c;
+                            const uint32_t col = (sc & 1) * D + oc0 + 32 * c;
                             uint32_t r[16];
                             tc::ld_16x32bx2_x16(tl + col, r);
                             tc::wait_ld();
@@ -647,82 +725,31 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                     tc::fence_before_sync();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(p_full + b));
+                    if (has_pend) {   // the previous segment's output, now that these weights are out
+                        has_pend = false;
+                        if (!finish(pend)) {
+                            stop = true;
+                            break;
+                        }
+                    }
                     ++gs;
                     j += n;
                 }
-                // the segment's output block, once its last PV products are done
-                if (!stop && o_live) {
-                    if (!warp_wait(p_free + ((gs - 1) & 1), ((gs - 1) >> 1) & 1)) {
-                        stop = true;
-                    } else {
-                        tc::fence_after_sync();
-#pragma unroll
-                        for (int c = 0; c < OCW; ++c) tc::ld_16x32bx2_x16(tl + S::O_COL + oc0 + 32 * c, ov[c]);
-                        tc::wait_ld();
-                    }
+                if (!stop) {
+                    pend = Seg{sg, g0, nh, gs - 1, sc & 1, m_ref, m_top, l, o_live, true};
+                    has_pend = true;
                 }
-                tc::fence_before_sync();
-                __syncwarp();
-                if (!stop && lane == 0) mbar_arrive(smem_u32(o_free));
+                ++sc;
+            } else if (npg == 0) {
+                // an empty sequence: zero rows, (m, l) = (-inf, 0)
+                if (!finish(Seg{sg, g0, nh, 0, 0, -INFINITY, -INFINITY, 0.f, false, false})) stop = true;
             }
             if (stop) {
                 if (lane == 0) fail_wait();
                 break;
             }
-            if (!o_live) {
-                l = 0.f;
-#pragma unroll
-                for (int c = 0; c < OCW; ++c)
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) ov[c][e] = 0u;
-            } else {
-                // the row's denominator: this warp's two halves, then both warps, added
-                // in warp order so that both hold the same bits
-                const float lw = l + __shfl_xor_sync(kFullMask, l, 16);
-                float *xr = xl + quad * 32;
-                if (half == 0) xr[cs * 16 + (lane & 15)] = lw;
-                if (!pair_sync()) {
-                    if (lane == 0) fail_wait();
-                    stop = true;
-                    break;
-                }
-                l = xr[lane & 15] + xr[16 + (lane & 15)];
-            }
-            // (m, l, o) against the true maximum, as the warp-level kernel writes them
-            const float f = m_top == -INFINITY ? 0.f : ex2_ftz(m_ref - m_top);
-            l *= f;
-            const bool mine = hrow < nh;
-            const int64_t qhead = int64_t(g0.x) * a.Hq + int64_t(g0.y) * a.group + g0.z + hrow;
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            if (sg.w < 0 && a.xworld) {
-                // the final row of this rank: to its slot in every rank's exchange buffer
-                for (int x = 0; x < a.xworld; ++x) {
-                    float *slot = xslot_of(a, x, xpar);
-                    if (mine) {
-                        store_o_part<OCW>(slot + qhead * D, ov, oc0, half, f * inv);
-                        if (cs == 0 && half == 0)
-                            *reinterpret_cast<float2 *>(xmeta_of<D>(slot, a, qhead)) = make_float2(m_top, l);
-                    }
-                }
-                // both warps' parts of these rows are stored: tag them
-                if (!pair_sync()) {
-                    if (lane == 0) fail_wait();
-                    stop = true;
-                    break;
-                }
-                if (cs == 0) publish_rows<D>(a, qhead - (lane & 15), max(0, min(16, nh - 16 * quad)), xpar, xe, lane);
-            } else {
-                // the group's only segment, seen whole by this CTA: final output;
-                // else the segment's (m, l, o) partial in slot sg.w
-                const int64_t pr = int64_t(sg.w) * GT + hrow;
-                if (mine) store_o_part<OCW>(sg.w < 0 ? a.out + qhead * D : a.part_o + pr * D, ov, oc0, half,
-                                            sg.w < 0 ? f * inv : f);
-                if (mine && cs == 0 && half == 0) {
-                    if (sg.w >= 0) a.part_ml[pr] = make_float2(m_top, l);
-                    else if (a.stats) reinterpret_cast<float2 *>(a.stats)[qhead] = make_float2(m_top, l);
-                }
-            }
         }
+        if (has_pend && !stop && !finish(pend) && lane == 0) fail_wait();
         tc::fence_before_sync();
     }
 

@@ -169,10 +169,17 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     p.total_pages = total;
 
     // ---------------------------------------------------------------- balance
+    // The warp-level kernels cost about the same per page tile: CTAs get equal
+    // page counts.  The tcgen05 kernel works in steps of 128 tokens of one
+    // segment and a step costs about the same whether full or not: CTAs get
+    // equal step counts, and cuts fall on step boundaries of the group.
+    const int64_t unit = p.engine == kEngineTensorMemory ? std::max(1, 128 / T) : 1;   // pages per unit
+    int64_t total_units = 0;
+    for (int64_t gi = 0; gi < ngroups; ++gi) total_units += (gpages[gi] + unit - 1) / unit;
     int64_t C = num_ctas > 0 ? num_ctas : std::max(1, sm_count);
-    C = std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total)));
+    C = std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total_units)));
     p.num_ctas = int32_t(C);
-    auto bound = [&](int64_t c) { return c * total / C; };   // start of CTA c's range
+    auto bound = [&](int64_t c) { return c * total_units / C; };   // start of CTA c's range, in units
     std::vector<std::vector<int32_t>> per(C);
     std::vector<int32_t> seg_count(ngroups, 0);
     int64_t cursor = 0, c = 0, empty = 0;
@@ -185,13 +192,14 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
             seg_count[gi] = 1;
             continue;
         }
+        const int64_t nu = (np + unit - 1) / unit;
         int64_t start = cursor;
-        const int64_t end = cursor + np;
+        const int64_t end = cursor + nu;
         while (start < end) {
             while (bound(c + 1) <= start) ++c;
             const int64_t stop = std::min(end, bound(c + 1));
-            per[c].insert(per[c].end(), {int32_t(gi), int32_t(start - cursor),
-                                         int32_t(stop - cursor), 0});
+            per[c].insert(per[c].end(), {int32_t(gi), int32_t((start - cursor) * unit),
+                                         int32_t(std::min(np, (stop - cursor) * unit)), 0});
             ++seg_count[gi];
             start = stop;
         }

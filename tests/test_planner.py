@@ -42,9 +42,15 @@ def check_worklist(layout, table, lengths, plan):
     assert offs[0] == 0 and offs[-1] == len(segs) and (np.diff(offs) >= 0).all()
     total = sum(-(-int(lengths[g[0]]) // T) for g in groups)
     assert info["total_pages"] == total
-    per_cta = [int((segs[offs[c]:offs[c + 1], 2] - segs[offs[c]:offs[c + 1], 1]).sum()) for c in range(C)]
-    if total:
-        assert min(per_cta) >= total // C and max(per_cta) <= -(-total // C)
+    # balance: equal page counts, or for the tcgen05 kernel equal counts of
+    # 128-token steps with cuts on step boundaries of the group
+    unit = 128 // T if info["engine"] == 1 else 1
+    per_cta = [sum(-(-int(s[2] - s[1]) // unit) for s in segs[offs[c]:offs[c + 1]]) for c in range(C)]
+    if unit > 1:
+        assert all(int(s[1]) % unit == 0 for s in segs)
+    units = sum(-(-(-(-int(lengths[g[0]]) // T)) // unit) for g in groups)
+    if units:
+        assert min(per_cta) >= units // C and max(per_cta) <= -(-units // C)
     stride = info["slot_stride"]
     # FP16 plans: consumer warps per tile = hg * gt/8 <= 8; sub-pipelines by tile size
     cpt = hg * gt // 8
@@ -166,3 +172,27 @@ def test_dynamic_plan_covers_each_sequence_up_to_its_capacity():
         inspect_plan(layout, table, lengths, num_ctas=7, max_lengths=np.array([60, 5, 161]))
     with pytest.raises(ValueError, match="max_lengths"):
         inspect_plan(layout, table, lengths, num_ctas=7, max_lengths=np.array([19, 5, 160]))
+
+
+@pytest.mark.parametrize("ctas", [1, 3, 7, 148, 1000])
+@pytest.mark.parametrize("kv_heads,heads,dim,page", [(1, 32, 128, 32), (1, 64, 64, 16), (2, 48, 128, 16)])
+def test_tcgen05_plans_cut_on_step_boundaries(ctas, kv_heads, heads, dim, page, monkeypatch):
+    """PD_MQA_ENGINE=tcgen05 plans balance 128-token steps, not pages: every cut
+    falls on a step boundary of its group and CTAs get equal step counts."""
+    monkeypatch.setenv("PD_MQA_ENGINE", "tcgen05")
+    rng = np.random.default_rng(ctas + heads)
+    lengths = np.array([0, 1, 129, 1000, 4096, 77], dtype=np.int32)
+    width = -(-int(lengths.max()) // page)
+    layout = Layout(len(lengths), heads, kv_heads, dim, page, len(lengths) * width)
+    table = rng.integers(0, layout.physical_pages, size=(len(lengths), width)).astype(np.int32)
+    plan = inspect_plan(layout, table, lengths, num_ctas=ctas)
+    assert plan["info"]["engine"] == 1
+    check_worklist(layout, table, lengths, plan)
+
+
+def test_tcgen05_plan_of_config_3b(monkeypatch):
+    monkeypatch.setenv("PD_MQA_ENGINE", "tcgen05")
+    w = workload.CONFIGS["c3b"]()
+    plan = inspect_plan(w.layout, w.table, w.lengths, split_tokens=w.split_tokens, num_ctas=148)
+    assert plan["info"]["engine"] == 1
+    check_worklist(w.layout, w.table, w.lengths, plan)

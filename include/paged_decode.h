@@ -86,9 +86,11 @@ typedef struct pd_plan_info {
     int64_t device_bytes;    /* everything pd_plan_bind needs (metadata + workspace) */
     int32_t engine;          /* consumer engine of the decode kernel: PD_ENGINE_WARP (every
                                 consumer warp runs m16n8k16 MMAs or FP32 FMAs) or
-                                PD_ENGINE_TCGEN05 (FP16 group tiles of 32 query heads when the
-                                environment has PD_MQA_ENGINE=tcgen05 at plan creation: single
-                                threads issue the MMAs into tensor memory) */
+                                PD_ENGINE_TCGEN05 (FP16 group tiles of 32 query heads, head_dim
+                                128, 32-token pages; any FP16 32-head tile when the environment
+                                has PD_MQA_ENGINE=tcgen05 at plan creation, none with
+                                PD_MQA_ENGINE=warp: single threads issue the MMAs into tensor
+                                memory) */
     int32_t reserved;
 } pd_plan_info;
 

@@ -133,12 +133,17 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         const int kib = std::atoi(env);
         if (kib >= 1) target = kib * 1024;
     }
-    // FP16 group tiles of 32 query heads run on the warp-level kernel
-    // (m16n8k16 MMAs, up to two KV heads per tile) unless PD_MQA_ENGINE=tcgen05
-    // selects the tcgen05 kernel (one KV head per page tile).
+    // FP16 group tiles of 32 query heads: the tcgen05 kernel (one KV head per
+    // page tile) where it measured faster than the warp-level kernel (m16n8k16
+    // MMAs, up to two KV heads per tile): head_dim 128 with 32-token pages
+    // (config 3b 24.8 against 25.4 us).  With 16-token pages it is slower (its
+    // steps carry twice the loads and PV products per byte).  PD_MQA_ENGINE=
+    // tcgen05 or warp forces either kernel for every such plan.
     const char *engine_env = std::getenv("PD_MQA_ENGINE");
-    const bool tensor_memory = dtype == PD_FLOAT16 && p.group_tile == 32 && engine_env &&
-                               std::strcmp(engine_env, "tcgen05") == 0;
+    const bool force_tc = engine_env && std::strcmp(engine_env, "tcgen05") == 0;
+    const bool force_warp = engine_env && std::strcmp(engine_env, "warp") == 0;
+    const bool tensor_memory = dtype == PD_FLOAT16 && p.group_tile == 32 && !force_warp &&
+                               (force_tc || (L.head_dim == 128 && T == 32));
     const int hg = tensor_memory ? 1
                                  : choose_heads_per_tile(dtype == PD_FLOAT16 ? 2 : 4, L.head_dim, T, p.group_tile,
                                                          L.kv_heads, target);
@@ -172,11 +177,17 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // The warp-level kernels cost about the same per page tile: CTAs get equal
     // page counts.  The tcgen05 kernel works in steps of 128 tokens of one
     // segment and a step costs about the same whether full or not: CTAs get
-    // equal step counts, and cuts fall on step boundaries of the group.
-    const int64_t unit = p.engine == kEngineTensorMemory ? std::max(1, 128 / T) : 1;   // pages per unit
+    // equal step counts, and cuts fall on step boundaries of the group, unless
+    // there are fewer than 4 steps per CTA (then more CTAs streaming part steps
+    // beat fewer streaming whole ones).
+    int64_t C = num_ctas > 0 ? num_ctas : std::max(1, sm_count);
+    int64_t unit = p.engine == kEngineTensorMemory ? std::max(1, 128 / T) : 1;   // pages per unit
     int64_t total_units = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) total_units += (gpages[gi] + unit - 1) / unit;
-    int64_t C = num_ctas > 0 ? num_ctas : std::max(1, sm_count);
+    if (unit > 1 && total_units < 4 * C) {
+        unit = 1;
+        total_units = total;
+    }
     C = std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total_units)));
     p.num_ctas = int32_t(C);
     auto bound = [&](int64_t c) { return c * total_units / C; };   // start of CTA c's range, in units

@@ -45,6 +45,8 @@ def check_worklist(layout, table, lengths, plan):
     # balance: equal page counts, or for the tcgen05 kernel equal counts of
     # 128-token steps with cuts on step boundaries of the group
     unit = 128 // T if info["engine"] == 1 else 1
+    if unit > 1 and sum(-(-(-(-int(lengths[g[0]]) // T)) // unit) for g in groups) < 4 * C:
+        unit = 1   # too few steps per CTA: balanced by pages
     per_cta = [sum(-(-int(s[2] - s[1]) // unit) for s in segs[offs[c]:offs[c + 1]]) for c in range(C)]
     if unit > 1:
         assert all(int(s[1]) % unit == 0 for s in segs)

@@ -1,9 +1,9 @@
 """The tcgen05 decode kernel for wide query groups (FP16, 17..32 query heads per KV head).
 
-With PD_MQA_ENGINE=tcgen05, FP16 plans whose group tile holds 32 query heads
-run on the kernel that issues its QK^T and PV products from single threads into
-tensor memory (csrc/pd_decode_mqa.cuh); by default they stay on the warp-level
-kernel.  The CPU tests pin the planner's choice (engine,
+FP16 plans whose group tile holds 32 query heads run on the kernel that issues
+its QK^T and PV products from single threads into tensor memory
+(csrc/pd_decode_mqa.cuh) by default for head_dim 128 with 32-token pages, and
+for every such shape with PD_MQA_ENGINE=tcgen05.  The CPU tests pin the planner's choice (engine,
 one KV head per page tile, one partial slot per segment).  The GPU tests check
 that kernel against the FP64 oracle on the shapes it serves (head_dim 64 and
 128, pages of 16 and 32 tokens, groups of 17, 24, 32 and 64 query heads per
@@ -52,11 +52,19 @@ def test_fp16_group_tiles_of_32_heads_choose_the_tcgen05_kernel(heads, kv_heads,
         assert fp16["group_tile"] == 32 and fp16["heads_per_tile"] == 1 and fp16["slot_stride"] == 1
 
 
-def test_the_warp_level_kernel_is_the_default(monkeypatch):
+def test_default_engine_and_overrides(monkeypatch):
+    """By default the tcgen05 kernel takes head_dim 128 with 32-token pages
+    (where it measured faster); PD_MQA_ENGINE=warp or tcgen05 forces a kernel."""
+    monkeypatch.delenv("PD_MQA_ENGINE", raising=False)
     layout, table, lengths = _fragmented(2, 32, 1, 128, 32, [500, 70])
-    monkeypatch.setenv("PD_MQA_ENGINE", "tcgen05")
     assert inspect_plan(layout, table, lengths)["info"]["engine"] == TCGEN05
-    monkeypatch.delenv("PD_MQA_ENGINE")
+    for dim, page in ((128, 16), (64, 32), (64, 16)):
+        small = _fragmented(2, 32, 1, dim, page, [500, 70])
+        assert inspect_plan(*small)["info"]["engine"] == 0
+        monkeypatch.setenv("PD_MQA_ENGINE", "tcgen05")
+        assert inspect_plan(*small)["info"]["engine"] == TCGEN05
+        monkeypatch.delenv("PD_MQA_ENGINE")
+    monkeypatch.setenv("PD_MQA_ENGINE", "warp")
     info = inspect_plan(layout, table, lengths)["info"]
     # two sub-pipelines of four warps on 16 KiB tiles, one partial slot each
     assert info["engine"] == 0 and info["heads_per_tile"] == 1 and info["slot_stride"] == 2
@@ -123,7 +131,7 @@ def test_tcgen05_kernel_is_repeatable_and_agrees_with_the_warp_kernel(dim, page)
     q, k, v = make_tensors(layout, seed=8)
     expected = _oracle(q, k, v, table, lengths)
     tc = _plan(layout, table, lengths)
-    warp = _plan(layout, table, lengths, engine=None)
+    warp = _plan(layout, table, lengths, engine="warp")
     assert tc.info.engine == TCGEN05 and warp.info.engine == 0
     first = tc.run(q, k, v).clone()
     for _ in range(3):

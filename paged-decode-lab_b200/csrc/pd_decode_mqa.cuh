@@ -69,11 +69,11 @@ struct MqaShape {
     static constexpr int P_BYTES = (GT / 8) * P_SBO;
     // An M = 64 MMA reads 64 rows of A; rows 32..63 (never read back from
     // tensor memory) come from whatever follows the 32 written rows, which
-    // must be allocated shared memory: P buffer 1 reads on into the Q
-    // buffers, Q buffer 1 into GUARD bytes after them.
+    // must be allocated shared memory: shared memory holds [P0][P1][Q0][Q1]
+    // [rings], so P buffer 1 reads on into the Q buffers and Q buffer 1 into
+    // the rings.
     static constexpr int P_READ = (M / 8) * P_SBO;                      // from a P buffer's start
     static constexpr int Q_READ = (NBOX - 1) * Q_BOX + (M / 8) * 1024;  // from a Q buffer's start
-    static constexpr int GUARD = Q_READ > Q_BYTES ? Q_READ - Q_BYTES : 0;
     // tensor-memory columns: output blocks [0, D) and [D, 2 D) (alternate segments),
     // score blocks [2 D, 2 D + NS), [2 D + NS, 2 D + 2 NS)
     static constexpr int S_COL = 2 * D;
@@ -89,7 +89,7 @@ struct MqaShape {
     // empty mbarriers and a valid word (20 bytes).
     static constexpr int KSTEP_BYTES = NBOX * NS * 128;
     static constexpr int KSS = 2;
-    static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + GUARD + NBARS * 8 +
+    static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + NBARS * 8 +
                                     XMAX_BYTES + XL_BYTES + 16 + 16 + 16 + size_t(KSS) * (KSTEP_BYTES + 20);
     static constexpr int VFIT = int((232448 - FIXED) / (HALF_BYTES + 20));
     static constexpr int VS = VFIT > 48 ? 48 : VFIT;
@@ -100,6 +100,7 @@ struct MqaShape {
     static_assert(T == 16 || T == 32, "page_size 16 or 32");
     static_assert(NS == 64 || NS == 128, "a step is 64 or 128 score columns");
     static_assert(P_READ <= P_BYTES + 2 * Q_BYTES, "P buffer 1's unread rows must stay inside the Q buffers");
+    static_assert(Q_READ <= Q_BYTES + size_t(KSS) * KSTEP_BYTES, "Q buffer 1's unread rows must stay inside the rings");
     static_assert(S_COL + 2 * NS <= TMEM_COLS, "tensor memory budget");
     static_assert(NP * (T * 128) % 1024 == 0 && (T * 128) % 1024 == 0, "pages keep 1024-byte swizzle atoms");
     // a step's V pages are released after its PV products: the V ring must
@@ -241,12 +242,12 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *ring = smem;
+    uint8_t *pbuf = smem;                                   // [2][P_BYTES]
+    uint8_t *qbuf = pbuf + 2 * S::P_BYTES;                  // [2][Q_BYTES]
+    uint8_t *ring = qbuf + 2 * S::Q_BYTES;
     uint8_t *kring = ring;                                  // [KSS][box][NS tokens][128 B]
     uint8_t *vring = ring + size_t(KSS) * S::KSTEP_BYTES;   // [VS][box][T tokens][128 B]
-    uint8_t *pbuf = ring + S::RING;
-    uint8_t *qbuf = pbuf + 2 * S::P_BYTES;
-    uint64_t *kfull = reinterpret_cast<uint64_t *>(qbuf + 2 * S::Q_BYTES + S::GUARD);
+    uint64_t *kfull = reinterpret_cast<uint64_t *>(ring + S::RING);
     uint64_t *kempty = kfull + KSS;
     uint64_t *vfull = kempty + KSS;
     uint64_t *vempty = vfull + VS;

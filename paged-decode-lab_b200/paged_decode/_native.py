@@ -15,6 +15,7 @@ PD_OK, PD_ERR_VALUE, PD_ERR_TYPE, PD_ERR_CUDA, PD_ERR_DEVICE, PD_ERR_UNBOUND = r
 PD_FLOAT16, PD_FLOAT32 = 0, 1
 PD_DEVERR_TIMEOUT, PD_DEVERR_BAD_PAGE = 1, 2
 PD_BARRIER_PLAIN, PD_BARRIER_COOPERATIVE, PD_BARRIER_LEAVE_AT_ONCE = 0, 1, 2
+PD_ENGINE_WARP, PD_ENGINE_TCGEN05 = 0, 1
 
 # Every function the header declares, with its ctypes signature.
 _c_int32, _c_int64, _c_size, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p

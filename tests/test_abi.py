@@ -162,3 +162,14 @@ def test_barrier_mode_and_counters_on_a_host_only_plan():
     assert lib.pd_selftest_barrier_leave(0, 0, outcomes) == _native.PD_ERR_VALUE        # leave_us 0
     assert lib.pd_selftest_barrier_leave(0, 200000, outcomes) == _native.PD_ERR_VALUE   # above 1e5
     assert lib.pd_selftest_barrier_leave(0, 200, None) == _native.PD_ERR_VALUE
+
+
+def test_header_constants_match_the_python_binding():
+    """Every #define the Python binding mirrors has the header's value."""
+    import re
+    from pathlib import Path
+    text = (Path(__file__).resolve().parents[1] / "include" / "paged_decode.h").read_text()
+    defines = {m.group(1): int(m.group(2), 0) for m in re.finditer(r"#define (PD_\w+) (0x[0-9a-fA-F]+|\d+)u?", text)}
+    for name in ("PD_ENGINE_WARP", "PD_ENGINE_TCGEN05", "PD_BARRIER_PLAIN", "PD_BARRIER_COOPERATIVE",
+                 "PD_BARRIER_LEAVE_AT_ONCE", "PD_DEVERR_TIMEOUT", "PD_DEVERR_BAD_PAGE"):
+        assert defines[name] == getattr(_native, name), name

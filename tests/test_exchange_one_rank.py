@@ -43,6 +43,9 @@ CASES = {
     # a few long sequences: teams of warps per row, plus short unsplit ones written directly
     "f16_p16_teams": (torch.float16, (4, 32, 8, 128, 16, [7000, 3, 0, 5000], 22)),
     "f32_d64_rows": (torch.float32, (8, 8, 8, 64, 16, [900, 2500, 1, 4000, 0, 300, 1700, 64], 23)),
+    # MQA tiles of 32 query heads on the tcgen05 kernel: its own exchange writes (two warps per row)
+    "f16_mqa_tcgen05": (torch.float16, (64, 32, 1, 128, 32, [2048] * 64, 24)),
+    "f16_mqa_tcgen05_ragged": (torch.float16, (8, 64, 1, 128, 32, [4000, 3, 0, 2000, 64, 700, 1, 5000], 25)),
 }
 
 
@@ -52,6 +55,8 @@ def test_one_rank_exchange_matches_the_plain_decode(name):
     layout, table, lengths = _case(*args)
     q, k, v = make_tensors(layout, dtype=dtype, seed=args[-1])
     plan = DecodePlan(layout, table, lengths)
+    if "tcgen05" in name:
+        assert plan.info.engine == _native.PD_ENGINE_TCGEN05
     ref = plan.run(q, k, v).clone()
     lib = _native.load()
     code = _native.PD_FLOAT16 if dtype == torch.float16 else _native.PD_FLOAT32

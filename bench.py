@@ -72,6 +72,8 @@ NCU_TRAFFIC_BYTES = {"c1": 67_258_880 + 571_648, "c2": 469_731_072 + 5_400_320,
                      "c3c": 540_718_336 + 4_886_528, "c5": 1_073_953_792 + 3_577_344}
 NCU_TRAFFIC_BYTES["c4s"] = 580_584_448 + 4_443_648
 NCU_SCALED = {"c4": ("c4s", NCU_TRAFFIC_BYTES["c4s"])}   # workload -> (captured workload, its traffic)
+# the same for plans on the tcgen05 kernel (paged_decode_mqa_kernel)
+NCU_TRAFFIC_BYTES_TCGEN05 = {"c3b": 67_816_960 + 1_204_992}
 
 
 def parse_args():
@@ -635,8 +637,12 @@ def run_ours(args, rank, local, world):
     kernel_ms = statistics.median(window_ms)
     achieved = job.bytes_rank / (kernel_ms * 1e-3) / 1e9
     traffic, traffic_note = None, None
+    info = job.decode_plan.native_info(q.dtype)
+    tcgen05 = int(info.engine) == 1
     if world == 1 or args.scaling == "weak":
-        if args.workload in NCU_TRAFFIC_BYTES:
+        if tcgen05:
+            traffic = NCU_TRAFFIC_BYTES_TCGEN05.get(args.workload)
+        elif args.workload in NCU_TRAFFIC_BYTES:
             traffic = NCU_TRAFFIC_BYTES[args.workload]
         elif args.workload in NCU_SCALED:
             from paged_decode import workload as wl
@@ -645,7 +651,6 @@ def run_ours(args, rank, local, world):
             traffic = int(src_traffic * ratio)
             traffic_note = (f"ncu capture of workload {src} ({src_traffic} B) scaled by the ratio of "
                             f"algorithmic bytes {ratio:.3f}")
-    info = job.decode_plan.native_info(q.dtype)
     line = {
         "metric": METRIC,
         "value": job.bytes_total / (step_ms * 1e-3) / 1e12,
@@ -666,7 +671,8 @@ def run_ours(args, rank, local, world):
                    "bytes_per_step_total": job.bytes_total, "bytes_per_step_rank": job.bytes_rank,
                    "sharding": job.sharding, "l2": l2, "timing": how,
                    "persistent_ctas": int(info.num_ctas),
-                   "kv_heads_per_tile": int(info.heads_per_tile)},
+                   "kv_heads_per_tile": int(info.heads_per_tile),
+                   "engine": "tcgen05" if tcgen05 else "warp"},
         "windows": {"count": args.windows, "steps_each": args.steps,
                     "median_us": step_ms * 1e3, "min_us": min(window_ms) * 1e3,
                     "p95_us": percentile(window_ms, 95) * 1e3,
@@ -675,8 +681,8 @@ def run_ours(args, rank, local, world):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic,
-                     "kernel": "paged_decode_kernel" + ("" if job.kernels_per_step() == 1
-                                                        else " (+ merge_partials_kernel)"),
+                     "kernel": ("paged_decode_mqa_kernel" if tcgen05 else "paged_decode_kernel")
+                               + ("" if job.kernels_per_step() == 1 else " (+ merge_partials_kernel)"),
                      "kernel_us": kernel_ms * 1e3,
                      "algorithmic_bytes_per_launch": job.bytes_rank},
         "gpu_launches": args.windows * args.steps * job.kernels_per_step(),

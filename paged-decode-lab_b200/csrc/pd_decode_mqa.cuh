@@ -1,43 +1,42 @@
 // pd_decode_mqa.cuh — the decode kernel for wide query groups (MQA-like:
 // 17..32 query heads per KV head, FP16) on the 5th-generation tensor cores.
 //
-// Same work list, page-tile ring, partials and merges as paged_decode_kernel
+// Same work list, partials and merges as paged_decode_kernel
 // (pd_decode_kernel.cuh; the reference's partial_decode + merge in
-// src/paged_decode/csrc/decode.cu:26-168), with the consumer side rebuilt
-// around tcgen05:
+// src/paged_decode/csrc/decode.cu:26-168), with the streaming and consumer
+// sides rebuilt around tcgen05.  A step is NP consecutive pages of one
+// segment (NS = NP * T = 128 score columns):
 //
-//   * warp 7 (producer) streams each page's K rows and V rows (one KV head)
-//     with TMA into two rings: K pages are free again once their scores are
-//     done, V pages once the step's PV products are;
+//   * warp 7 (producer): lane 0 streams K a step at a time into step slots
+//     laid out [128-byte column][NS tokens][128 B], lane 1 each page's V into
+//     page slots; the lanes walk the work list independently;
 //   * warp 2 stages each segment's 32 query rows in shared memory (128-byte
 //     swizzled, K-major) two segments ahead;
 //   * one thread of warp 3 issues S = Q K^T for a whole step once its K has
-//     landed (M = 64 rows of which the 32 query heads are 0..31, N = the
-//     step's NS tokens, K = head dim: one MMA per 16 head dims) into a
-//     double-buffered score block in tensor memory; one thread of
-//     warp 6, once a step's weights P are in shared memory, issues O += P V
-//     (N = head dim) into an output block in tensor memory.  Two issuing
-//     threads, so that neither kind waits for the other's inputs (K landing,
-//     weights written);
+//     landed (M = 64 rows of which the 32 query heads are 0..31, N = NS, K =
+//     16 head dims per MMA) into one of two score blocks in tensor memory;
+//     one thread of warp 6, once a step's weights P are in shared memory,
+//     issues O += P V page by page as V lands (N = head dim) into one of two
+//     output blocks (consecutive segments alternate).  Two issuing threads,
+//     so that neither kind waits for the other's inputs;
 //   * warps 0 and 4 own query heads 0..15, warps 1 and 5 heads 16..31
 //     (tensor-memory lanes 0..15 of sub-partitions 0 and 1); of each step's
-//     NS score columns a warp takes one half, two threads per head.  Online
-//     softmax in base 2 with a lazily moved reference maximum: the two warps
-//     of a head trade their row maxima each step, and only a maximum that
-//     passes the reference by more than 2^8 moves it (and rescales the output
-//     block), so weights stay <= 256 in FP16.  At each segment end the output
-//     block comes back from tensor memory and is written out exactly as the
-//     warp-level kernel writes it (final row, exchange row or (m, l, o)
+//     columns a warp takes one half, two threads per head.  Online softmax in
+//     base 2 with a lazily moved reference maximum: the two warps of a head
+//     trade their row maxima each step, and only a maximum that passes the
+//     reference by more than 2^8 moves it (and rescales the output block), so
+//     weights stay <= 256 in FP16.  A segment's output block is read back
+//     once the next segment's first weights are out and written exactly as
+//     the warp-level kernel writes it (final row, exchange row or (m, l, o)
 //     partial, m the true maximum).
 //
-// A step is NP consecutive pages of one segment (NS = NP * T score columns).
-// mbarriers order the roles: K and V ring full/empty (TMA -> score / PV
+// mbarriers order the roles: K and V slot full/empty (TMA -> score / PV
 // MMAs), q_full/q_empty (query rows), s_full (scores ready), p_full (weights
 // written), p_free (the step's PV products done: its weights and V pages are
-// free, the output block quiescent), o_free (a segment's output read back),
-// pair (the two softmax warps of the same heads).  Every wait is bounded; on a timeout the
-// CTA records PD_DEVERR_TIMEOUT, unwinds, waits for its own MMAs and frees its
-// tensor memory.
+// free), o_free (an output block read back), pair (the two softmax warps of
+// the same heads).  Every wait is bounded; on a timeout the CTA records
+// PD_DEVERR_TIMEOUT, unwinds, waits for its own MMAs and frees its tensor
+// memory.
 #pragma once
 
 #include "pd_decode_kernel.cuh"
@@ -372,7 +371,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t ID_S = tc::idesc_f16_f32(S::M, NS, false, false);   // Q, K: K-major
             bool stop = false;
-            int gs = 0, j = 0, sc = 0;
+            int gs = 0, sc = 0;
             for (int si = seg_begin; si < seg_end && !stop; ++si) {
                 const int4 sg = si == seg_begin ? sg_h : a.segs[si];
                 const int npg = sg.z - sg.y;
@@ -411,13 +410,11 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         }
                     }
                     tc::commit(smem_u32(kempty + ks));   // the step's K, once these scores are done
-                    if (stop) break;
                     tc::commit(smem_u32(s_full + b));
                     svalid[b] = valid;
                     mbar_arrive(smem_u32(s_full + b));
                     if (p0 + NP >= npg) tc::commit(smem_u32(q_empty + qb));   // the segment's query rows
                     ++gs;
-                    j += n;
                 }
                 ++sc;
             }

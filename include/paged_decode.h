@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PD_ABI_VERSION 7
+#define PD_ABI_VERSION 8
 
 typedef enum pd_status {
     PD_OK = 0,
@@ -91,7 +91,14 @@ typedef struct pd_plan_info {
                                 has PD_MQA_ENGINE=tcgen05 at plan creation, none with
                                 PD_MQA_ENGINE=warp: single threads issue the MMAs into tensor
                                 memory) */
-    int32_t reserved;
+    int32_t cluster_ctas;    /* CTAs per thread-block cluster of the decode launch: 1, or 2 for a
+                                pair plan (tcgen05 engine, num_ctas <= 0 at creation, groups of
+                                near-equal length that fill at least 3/4 of the SMs two CTAs
+                                each; PD_PAIR=0 / 1 in the environment at plan creation turns
+                                it off / on wherever the groups fit): the two CTAs of a cluster
+                                stream the two halves of one group and merge them through
+                                distributed shared memory, with no partials, grid barrier or
+                                merge kernel.  pd_decode_exchange rejects pair plans. */
 } pd_plan_info;
 
 #define PD_ENGINE_WARP 0
@@ -107,7 +114,8 @@ typedef struct pd_plan_info {
  * the page tiles it gathers are sized for it (the Python DecodePlan keeps one
  * plan per dtype behind its dtype-agnostic run()).  device < 0 builds a
  * host-only plan (inspection, no decode).  num_ctas <= 0 picks one CTA per SM
- * of device.
+ * of device, or two CTAs per group in clusters of two (a pair plan, see
+ * pd_plan_info.cluster_ctas).
  */
 pd_status pd_plan_create(const pd_layout *layout, const int32_t *table, int64_t table_width,
                          const int32_t *lengths, int32_t split_tokens, int32_t merge_mode,
@@ -302,7 +310,8 @@ int32_t pd_abi_version(void);
  * Every rank must call it once per step, in the same order, with buffers[s] =
  * rank s's buffer as seen from this GPU (buffers[rank] = its own); at most
  * 1024 CTAs per rank.  No multicast and no library kernel touches peer
- * memory.
+ * memory.  A pair plan (pd_plan_info.cluster_ctas == 2) is rejected with
+ * PD_ERR_VALUE: create exchange plans with num_ctas > 0.
  */
 size_t pd_exchange_bytes(const pd_plan *plan, int32_t world);
 pd_status pd_exchange_alloc(int32_t device, size_t bytes, void **buffer, void *ipc_handle /* 64 bytes */);

@@ -195,6 +195,7 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     const auto st = static_cast<cudaStream_t>(stream);
     DecodeArgs la = args;
     if (mode != kModeDecode) la.fused_merge = 0;
+    la.pair = mode == kModeDecode && p->cluster == 2 ? 1 : 0;
     // Every decode launch is programmatically dependent on the kernel before
     // it (the kernel waits with griddepcontrol.wait before touching q, the
     // caches or its outputs), so its launch and set-up overlap that kernel.
@@ -210,6 +211,19 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     attr[1].val.cooperative = 1;
     cfg.attrs = attr;
     cudaError_t err;
+    if (la.pair) {
+        // clusters of two CTAs (one group each); they wait only for each other
+        if (la.xworld || la.fused_merge) return fail(PD_ERR_VALUE, "a pair plan cannot take part in an exchange");
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+        err = cudaLaunchKernelEx(&cfg, e.fn, tc.map_k, tc.map_v, la);
+        if (err != cudaSuccess)
+            return fail(PD_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(err));
+        return PD_OK;
+    }
     if (la.fused_merge && !la.xworld && p->barrier_mode != PD_BARRIER_COOPERATIVE) {
         // A plain launch starts on SMs as the previous kernel's CTAs leave
         // them (measured 2-3 us a step ahead of a cooperative launch).  The
@@ -346,7 +360,7 @@ PD_API pd_status pd_plan_get_info(const pd_plan *p, pd_plan_info *info) {
     info->heads_per_tile = p->heads_per_tile;
     info->slot_stride = p->slot_stride;
     info->engine = p->engine;
-    info->reserved = 0;
+    info->cluster_ctas = p->cluster;
     info->total_pages = int32_t(p->total_pages);
     info->merge_rows = int32_t(p->merge_rows.size() / 4);
     info->merge_in_kernel = p->merge_in_kernel ? 1 : 0;
@@ -689,6 +703,8 @@ PD_API pd_status pd_decode_exchange(pd_plan *p, const void *q, const void *k, co
         if (!buffers[s] || (reinterpret_cast<uintptr_t>(buffers[s]) & 255))
             return fail(PD_ERR_VALUE, "exchange buffers must be non-NULL and 256-byte aligned");
     if (p->num_ctas > 1024) return fail(PD_ERR_VALUE, "exchange mode supports at most 1024 CTAs per rank");
+    if (p->cluster != 1)
+        return fail(PD_ERR_VALUE, "exchange mode needs a plan without CTA pairs (create it with num_ctas > 0)");
     DecodeArgs x{};
     for (int s = 0; s < world; ++s) x.xpeer[s] = static_cast<uint8_t *>(buffers[s]);
     x.xslot = exchange_slot_bytes(p);

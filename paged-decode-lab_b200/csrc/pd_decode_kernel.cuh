@@ -63,6 +63,7 @@ struct DecodeArgs {
     const int4 *merge_rows;      // split groups' rows: {out row, slot0, segments, head * GT + query head}
     int32_t num_merge_rows;
     int32_t fused_merge;         // 1: the CTAs merge the partials after a grid barrier
+    int32_t pair;                // 1: clusters of two CTAs split each group and merge it themselves
     // Dynamic plans: groups cover each sequence up to its capacity (group word
     // 4); the live length of sequence b is min(lengths[b], capacity), pages at
     // or past it are skipped, and page ids always come from `table`.

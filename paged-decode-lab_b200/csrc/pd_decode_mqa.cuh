@@ -30,6 +30,13 @@
 //     the warp-level kernel writes it (final row, exchange row or (m, l, o)
 //     partial, m the true maximum).
 //
+// Pair plans launch clusters of two CTAs that stream the two halves of one
+// group: each sends the partial (m, l, o) rows of the partner's 16 query heads
+// into the partner's shared memory (its unused second query buffer) and
+// keeps its own in weight buffer 0; after a cluster barrier each merges its
+// 16 heads and writes the final rows, with no partials in global memory, no
+// grid barrier and no merge kernel.
+//
 // mbarriers order the roles: K and V slot full/empty (TMA -> score / PV
 // MMAs), q_full/q_empty (query rows), s_full (scores ready), p_full (weights
 // written), p_free (the step's PV products done: its weights and V pages are
@@ -80,6 +87,7 @@ struct MqaShape {
     static constexpr int NBARS = 20;   // s_full, p_full, p_free, q_full, q_empty, o_free, mma_done: 2 each; pair: 4
     static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] row maxima
     static constexpr int XL_BYTES = 2 * 2 * 16 * 4;         // [heads half][warp][row] denominators
+    static constexpr int PAIR_ML_BYTES = 2 * 16 * 8;        // pair plans: (m, l) of 16 rows, own and received
     // K arrives a step at a time into KSS step slots laid out [box][NS tokens]
     // [128 B], so one MMA takes a whole step's scores per 16 head dims; a step
     // slot is free once those scores are done.  V arrives a page at a time
@@ -89,7 +97,7 @@ struct MqaShape {
     static constexpr int KSTEP_BYTES = NBOX * NS * 128;
     static constexpr int KSS = 2;
     static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + NBARS * 8 +
-                                    XMAX_BYTES + XL_BYTES + 16 + 16 + 16 + size_t(KSS) * (KSTEP_BYTES + 20);
+                                    PAIR_ML_BYTES + XMAX_BYTES + XL_BYTES + 16 + 16 + 16 + size_t(KSS) * (KSTEP_BYTES + 20);
     static constexpr int VFIT = int((232448 - FIXED) / (HALF_BYTES + 20));
     static constexpr int VS = VFIT > 48 ? 48 : VFIT;
     static constexpr size_t RING = size_t(KSS) * KSTEP_BYTES + size_t(VS) * HALF_BYTES;   // [K steps][V pages]
@@ -105,6 +113,8 @@ struct MqaShape {
     // a step's V pages are released after its PV products: the V ring must
     // hold two steps at once, and then some to stream ahead
     static_assert(VS >= 2 * NP + 2, "V ring too small for the steps in flight");
+    // pair plans: 16 rows of D FP32 outputs in weight buffer 0 (own) and query buffer 1 (received)
+    static_assert(16 * D * 4 <= P_BYTES && 16 * D * 4 <= Q_BYTES, "pair rows must fit their buffers");
     static_assert(SMEM <= 232448 && SMEM > 116 * 1024,
                   "one CTA per SM: its tensor memory is never contended by a second CTA of the grid");
 };
@@ -258,7 +268,8 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     uint64_t *pair_bar = q_empty + 2;       // [2 heads halves][2 phases]
     uint64_t *o_free = pair_bar + 4;        // [2] per output block
     uint64_t *mma_done = o_free + 2;        // [2] score MMAs, PV MMAs
-    float *xmax = reinterpret_cast<float *>(mma_done + 2);
+    float2 *pair_ml = reinterpret_cast<float2 *>(mma_done + 2);   // pair plans: [own, received][16 rows]
+    float *xmax = reinterpret_cast<float *>(pair_ml + 32);
     float *xl = xmax + S::XMAX_BYTES / 4;
     unsigned *svalid = reinterpret_cast<unsigned *>(xl + S::XL_BYTES / 4);   // [2]: pages streamed, per score block
     unsigned *kvalid = svalid + 4;                                           // [KSS]: pages streamed, per K step
@@ -304,6 +315,10 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // pair plans: this CTA's rank in its cluster; both CTAs have started (their
+    // shared memory may be written by the partner) once the barrier passes
+    const uint32_t prank = a.pair ? cluster_ctarank() : 0u;
+    if (a.pair) cluster_sync_all();
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (a.fused_merge && threadIdx.x == 0) atomicAdd(a.gb.started, 1ull);
@@ -315,6 +330,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         stream_mqa_pages<T, NP, NS, S::NBOX, HALF, S::KSTEP_BYTES, KSS, VS>(
             &tm_k, &tm_v, a, kring, vring, kfull, kempty, vfull, vempty, kvalid, vvalid, flags, seg_begin, seg_end,
             lane);
+        if (a.pair) cluster_sync_all();   // the partner's merge waits for every thread of both CTAs
         return;
     }
 
@@ -546,6 +562,20 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
             const float f = q.m_top == -INFINITY ? 0.f : ex2_ftz(q.m_ref - q.m_top);
             l *= f;
             const bool mine = hrow < q.nh;
+            if (a.pair) {
+                // heads 16 prank .. + 15 stay in weight buffer 0 (free: the last PV
+                // products are done), the others go to the partner's query buffer 1
+                const bool own = quad == int(prank);
+                float *rows = reinterpret_cast<float *>(own ? pbuf : qbuf + S::Q_BYTES);
+                float2 *ml = pair_ml + (own ? 0 : 16);
+                if (!own) {
+                    rows = cluster_map(rows, prank ^ 1u);
+                    ml = cluster_map(ml, prank ^ 1u);
+                }
+                if (mine) store_o_part<OCW>(rows + (lane & 15) * D, ov, oc0, half, f);
+                if (mine && cs == 0 && half == 0) ml[lane & 15] = make_float2(q.m_top, l);
+                return true;
+            }
             const int64_t qhead = int64_t(q.g0.x) * a.Hq + int64_t(q.g0.y) * a.group + q.g0.z + hrow;
             const float inv = l > 0.f ? 1.f / l : 0.f;
             if (q.sg.w < 0 && a.xworld) {
@@ -756,6 +786,41 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     if (warp == S::W_MMA) {
         tc::fence_after_sync();
         tc::dealloc(tmem, S::TMEM_COLS);
+    }
+    if (a.pair) {
+        // both halves' rows are in place once every thread of the pair is here
+        cluster_sync_all();
+        if ((warp == 0 || warp == 1 || warp == 4 || warp == 5) && (warp & 3) == int(prank)) {
+            const int cs = warp >> 2, half = lane >> 4, r = lane & 15;
+            const int hrow = 16 * int(prank) + r;
+            if (hrow < g0_h.w) {
+                const float2 mo = pair_ml[r], mp = pair_ml[16 + r];
+                const float mx = fmaxf(mo.x, mp.x);
+                const float wo = mo.x == -INFINITY ? 0.f : ex2_ftz(mo.x - mx);
+                const float wp = mp.x == -INFINITY ? 0.f : ex2_ftz(mp.x - mx);
+                const float l = fmaf(mo.y, wo, mp.y * wp);
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                const float so = wo * inv, sp = wp * inv;
+                const float *ro = reinterpret_cast<const float *>(pbuf) + r * D;
+                const float *rp = reinterpret_cast<const float *>(qbuf + S::Q_BYTES) + r * D;
+                const int64_t qhead = int64_t(g0_h.x) * a.Hq + int64_t(g0_h.y) * a.group + g0_h.z + hrow;
+                float *dst = a.out + qhead * D;
+#pragma unroll
+                for (int c = 0; c < OCW; ++c)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4) {
+                        const int col = cs * (D / 2) + 32 * c + 16 * half + e;
+                        const float4 x = *reinterpret_cast<const float4 *>(ro + col);
+                        const float4 y = *reinterpret_cast<const float4 *>(rp + col);
+                        *reinterpret_cast<float4 *>(dst + col) =
+                            make_float4(fmaf(x.x, so, y.x * sp), fmaf(x.y, so, y.y * sp), fmaf(x.z, so, y.z * sp),
+                                        fmaf(x.w, so, y.w * sp));
+                    }
+                if (a.stats && cs == 0 && half == 0) reinterpret_cast<float2 *>(a.stats)[qhead] = make_float2(mx, l);
+            }
+        }
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        return;
     }
     finish_decode<D, 1, GT, 1, NC, S::RING>(a, ring, flags, warp, lane, xpar, xe);
     if (a.fused_merge || a.xworld) return;

@@ -87,6 +87,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
     }
 }
 
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of every CTA of the cluster arrives (releasing its earlier
+// writes, distributed shared memory included) and waits for all the others.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Generic address of the same shared-memory location in CTA `rank` of this
+// cluster (ordinary loads and stores reach it).
+template <typename P>
+__device__ __forceinline__ P *cluster_map(P *p, uint32_t rank) {
+    uint64_t r;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+    return reinterpret_cast<P *>(r);
+}
+
 // ---------------------------------------------------------------- TMA
 // 5-D tiled load into CTA shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,

@@ -182,19 +182,45 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // beat fewer streaming whole ones).
     int64_t C = num_ctas > 0 ? num_ctas : std::max(1, sm_count);
     int64_t unit = p.engine == kEngineTensorMemory ? std::max(1, 128 / T) : 1;   // pages per unit
+    // Pair plans (tcgen05 engine, automatic CTA count): when the groups are
+    // about equally long and two CTAs per group fill most of the SMs, CTAs
+    // 2g and 2g + 1 form a cluster that streams the two halves of group g (cut
+    // on a step boundary) and merges them through distributed shared memory:
+    // no partials, no grid barrier, no merge kernel.  PD_PAIR=0 / 1 turns
+    // the choice off / on wherever the groups fit.
+    p.cluster = 1;
+    if (p.engine == kEngineTensorMemory && num_ctas <= 0 && sm_count > 0 && ngroups >= 1 &&
+        2 * ngroups <= std::min(sm_count, 1024)) {
+        int64_t longest = 0;
+        for (int64_t gi = 0; gi < ngroups; ++gi) longest = std::max(longest, gpages[gi]);
+        bool pair = longest * ngroups * 8 <= total * 9 && 2 * ngroups * 4 >= int64_t(sm_count) * 3;
+        if (const char *env = std::getenv("PD_PAIR")) {
+            if (std::strcmp(env, "0") == 0) pair = false;
+            if (std::strcmp(env, "1") == 0) pair = true;
+        }
+        if (pair) p.cluster = 2;
+    }
     int64_t total_units = 0;
     for (int64_t gi = 0; gi < ngroups; ++gi) total_units += (gpages[gi] + unit - 1) / unit;
-    if (unit > 1 && total_units < 4 * C) {
+    if (unit > 1 && total_units < 4 * C && p.cluster == 1) {
         unit = 1;
         total_units = total;
     }
-    C = std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total_units)));
+    C = p.cluster == 2 ? 2 * ngroups : std::max<int64_t>(1, std::min<int64_t>(C, std::max<int64_t>(1, total_units)));
     p.num_ctas = int32_t(C);
     auto bound = [&](int64_t c) { return c * total_units / C; };   // start of CTA c's range, in units
     std::vector<std::vector<int32_t>> per(C);
     std::vector<int32_t> seg_count(ngroups, 0);
     int64_t cursor = 0, c = 0, empty = 0;
-    for (int64_t gi = 0; gi < ngroups; ++gi) {
+    for (int64_t gi = 0; gi < ngroups && p.cluster == 2; ++gi) {
+        // the first CTA takes the first half of the group's steps (rounded up)
+        const int64_t np = gpages[gi];
+        const int64_t cut = std::min(np, ((np + unit - 1) / unit + 1) / 2 * unit);
+        per[2 * gi] = {int32_t(gi), 0, int32_t(cut), 0};
+        per[2 * gi + 1] = {int32_t(gi), int32_t(cut), int32_t(np), 0};
+        seg_count[gi] = 2;
+    }
+    for (int64_t gi = 0; gi < ngroups && p.cluster == 1; ++gi) {
         const int64_t np = gpages[gi];
         if (np == 0) {
             // empty sequence: a zero-page segment writes its zero rows
@@ -234,7 +260,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     for (int64_t gi = 0; gi < ngroups; ++gi) {
         int32_t *g = &p.groups[size_t(gi) * 8];
         g[6] = seg_count[gi];
-        if (seg_count[gi] == 1 && p.slot_stride == 1) {
+        if (p.cluster == 2 || (seg_count[gi] == 1 && p.slot_stride == 1)) {
             g[5] = -1;
         } else {
             g[5] = int32_t(slots);

@@ -49,6 +49,7 @@ struct pd_plan {
     int32_t heads_per_tile = 1;    // HG: KV heads gathered per page tile
     int32_t engine = 0;            // consumer engine of the decode kernel (kEngine*)
     int32_t num_ctas = 0;
+    int32_t cluster = 1;           // CTAs per cluster: 2 for a pair plan (two halves of each group)
     int32_t splits = 1;
     int32_t max_context = 0;
     int32_t num_pieces = 0;        // partial slots (segments that write partials x slot_stride)

@@ -37,7 +37,7 @@ class PlanInfo(ctypes.Structure):
                 ("merge_rows", ctypes.c_int32), ("merge_in_kernel", ctypes.c_int32),
                 ("dynamic", ctypes.c_int32), ("max_span", ctypes.c_int32),
                 ("workspace_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64),
-                ("engine", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("engine", ctypes.c_int32), ("cluster_ctas", ctypes.c_int32)]
 
 
 SIGNATURES = {
@@ -93,7 +93,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pd_abi_version() != 7:
+        if lib.pd_abi_version() != 8:
             raise RuntimeError("paged_decode native ABI version mismatch")
         _lib = lib
     return _lib

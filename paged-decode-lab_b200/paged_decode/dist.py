@@ -170,6 +170,9 @@ class SequenceShardedPlan:
         self.layout = layout
         self.exchange = exchange
         table, lengths = validate_metadata(layout, table, lengths)
+        if num_ctas is None and exchange == "peer":
+            # one CTA per SM: the exchange kernel takes no CTA-pair plans
+            num_ctas = torch.cuda.get_device_properties(torch.device(device)).multi_processor_count
         self.plan = DecodePlan(layout, table, lengths, device=device, split_tokens=split_tokens,
                                merge=merge, num_ctas=num_ctas)
         self.device = self.plan.device

@@ -40,7 +40,7 @@ def test_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _native.load()
-    assert lib.pd_abi_version() == 7
+    assert lib.pd_abi_version() == 8
     assert lib.pd_status_string(0) == b"ok"
     assert lib.pd_status_string(2) == b"invalid dtype"
 

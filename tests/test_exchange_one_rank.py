@@ -54,7 +54,8 @@ def test_one_rank_exchange_matches_the_plain_decode(name):
     dtype, args = CASES[name]
     layout, table, lengths = _case(*args)
     q, k, v = make_tensors(layout, dtype=dtype, seed=args[-1])
-    plan = DecodePlan(layout, table, lengths)
+    # exchange plans take one CTA per SM (num_ctas > 0: no CTA-pair plan)
+    plan = DecodePlan(layout, table, lengths, num_ctas=torch.cuda.get_device_properties(0).multi_processor_count)
     if "tcgen05" in name:
         assert plan.info.engine == _native.PD_ENGINE_TCGEN05
     ref = plan.run(q, k, v).clone()

@@ -90,18 +90,21 @@ struct MqaShape {
     static constexpr int PAIR_ML_BYTES = 2 * 16 * 8;        // pair plans: (m, l) of 16 rows, own and received
     // K arrives a step at a time into KSS step slots laid out [box][NS tokens]
     // [128 B], so one MMA takes a whole step's scores per 16 head dims; a step
-    // slot is free once those scores are done.  V arrives a page at a time
-    // into VS page slots and is free once its step's PV products are; the V
-    // ring holds two steps and streams ahead with the rest.  Per slot: full and
-    // empty mbarriers and a valid word (20 bytes).
+    // slot is free once those scores are done.  V also arrives a step at a time
+    // (its NP pages on one mbarrier, [page][box][T tokens][128 B]) into VSS
+    // step slots, each free once its PV products are done; the V ring holds two
+    // steps and streams ahead with the rest.  A TMA stream refilled one 8 KiB
+    // page per mbarrier reached about 19 GB/s per SM, four pages per mbarrier
+    // 45 GB/s.  Per slot: full and empty mbarriers and a valid-page mask (20 bytes).
     static constexpr int KSTEP_BYTES = NBOX * NS * 128;
+    static constexpr int VSTEP_BYTES = NP * HALF_BYTES;
     static constexpr int KSS = 2;
     static constexpr size_t FIXED = 1024 + 2 * size_t(P_BYTES) + 2 * size_t(Q_BYTES) + NBARS * 8 +
                                     PAIR_ML_BYTES + XMAX_BYTES + XL_BYTES + 16 + 16 + 16 + size_t(KSS) * (KSTEP_BYTES + 20);
-    static constexpr int VFIT = int((232448 - FIXED) / (HALF_BYTES + 20));
-    static constexpr int VS = VFIT > 48 ? 48 : VFIT;
-    static constexpr size_t RING = size_t(KSS) * KSTEP_BYTES + size_t(VS) * HALF_BYTES;   // [K steps][V pages]
-    static constexpr size_t SMEM = FIXED + size_t(VS) * (HALF_BYTES + 20);
+    static constexpr int VFIT = int((232448 - FIXED) / (VSTEP_BYTES + 20));
+    static constexpr int VSS = VFIT * NP > 48 ? 48 / NP : VFIT;   // V step slots (at most 48 pages)
+    static constexpr size_t RING = size_t(KSS) * KSTEP_BYTES + size_t(VSS) * VSTEP_BYTES;   // [K steps][V steps]
+    static constexpr size_t SMEM = FIXED + size_t(VSS) * (VSTEP_BYTES + 20);
 
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
     static_assert(T == 16 || T == 32, "page_size 16 or 32");
@@ -112,7 +115,7 @@ struct MqaShape {
     static_assert(NP * (T * 128) % 1024 == 0 && (T * 128) % 1024 == 0, "pages keep 1024-byte swizzle atoms");
     // a step's V pages are released after its PV products: the V ring must
     // hold two steps at once, and then some to stream ahead
-    static_assert(VS >= 2 * NP + 2, "V ring too small for the steps in flight");
+    static_assert(VSS >= 3, "V ring too small for the steps in flight");
     // pair plans: 16 rows of D FP32 outputs in weight buffer 0 (own) and query buffer 1 (received)
     static_assert(16 * D * 4 <= P_BYTES && 16 * D * 4 <= Q_BYTES, "pair rows must fit their buffers");
     static_assert(SMEM <= 232448 && SMEM > 116 * 1024,
@@ -129,6 +132,21 @@ __device__ __forceinline__ void store_o_part(float *dst, const uint32_t (&ov)[OC
 #pragma unroll
         for (int e = 0; e < 16; e += 4)
             *reinterpret_cast<float4 *>(dst + c0 + 32 * c + 16 * half + e) =
+                make_float4(__uint_as_float(ov[c][e]) * scale, __uint_as_float(ov[c][e + 1]) * scale,
+                            __uint_as_float(ov[c][e + 2]) * scale, __uint_as_float(ov[c][e + 3]) * scale);
+}
+
+// Pair plans: the same share of row r (< 16) of a 16-row block, with row r's
+// 16-byte chunk k stored at chunk k ^ r, so that the sixteen rows' threads
+// storing (or, in the merge, loading) the same columns reach distinct banks.
+template <int OCW>
+__device__ __forceinline__ void store_pair_row(float *row, int r, const uint32_t (&ov)[OCW][16], int c0, int half,
+                                               float scale) {
+#pragma unroll
+    for (int c = 0; c < OCW; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(row + 4 * (((c0 + 32 * c + 16 * half + e) >> 2) ^ r)) =
                 make_float4(__uint_as_float(ov[c][e]) * scale, __uint_as_float(ov[c][e + 1]) * scale,
                             __uint_as_float(ov[c][e + 2]) * scale, __uint_as_float(ov[c][e + 3]) * scale);
 }
@@ -152,16 +170,17 @@ __device__ __forceinline__ float ex2_ftz(float x) {
 //   lane 0, K by steps (NP consecutive pages of one segment): step s into step
 //     slot s % KSS, one TMA load per page and 128-byte column (page p, column b
 //     at b * NS * 128 + p * T * 128), once the scores of step s - KSS are done;
-//   lane 1, V by pages: page j's rows into V slot j % VS (one load,
-//     [column][token]) once the PV products of page j - VS are done.
+//   lane 1, V by steps: step s into V step slot s % VSS, one TMA load per
+//     page ([column][token], page p at p * HALF_BYTES), once the PV products
+//     of step s - VSS are done.
 // Pages past a dynamic plan's live length, or with an id outside the cache,
-// land nothing and are marked invalid (K: a bit per page of the step; V: per
-// slot).  Waits poll without suspending: the two lanes share one warp.
-template <int T, int NP, int NS, int NBOX, int HALF_BYTES, int KSTEP_BYTES, int KSS, int VS>
+// land nothing and are marked invalid (a bit per page of the step).  Waits
+// poll without suspending: the two lanes share one warp.
+template <int T, int NP, int NS, int NBOX, int HALF_BYTES, int KSTEP_BYTES, int KSS, int VSS>
 __device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const CUtensorMap *tm_v,
                                                  const DecodeArgs &a, uint8_t *kring, uint8_t *vring,
                                                  uint64_t *kfull, uint64_t *kempty, uint64_t *vfull,
-                                                 uint64_t *vempty, unsigned *kvalid, int *vvalid,
+                                                 uint64_t *vempty, unsigned *kvalid, unsigned *vvalid,
                                                  SmemFlags *flags, int seg_begin, int seg_end, int lane) {
     if (lane > 1) return;
     tma_prefetch_descriptor(lane == 0 ? tm_k : tm_v);
@@ -184,7 +203,7 @@ __device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const 
     const auto page_state = [&](int id, int64_t first_token, int live_end) {
         return first_token >= live_end ? 1 : (id >= 0 && int64_t(id) < a.P) ? 0 : 2;
     };
-    int gs = 0, j = 0;
+    int gs = 0;
     for (int si = seg_begin; si < seg_end; ++si) {
         const int4 sg = __ldg(a.segs + si);
         const int npg = sg.z - sg.y;
@@ -194,17 +213,17 @@ __device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const 
         const int live_end = a.dynamic ? max(0, a.lengths[g0.x]) : INT_MAX;
         for (int p0 = 0; p0 < npg; p0 += NP) {
             const int n = min(NP, npg - p0);
+            int ids[NP];
+            unsigned mask = 0;
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                ids[p] = p < n ? __ldg(trow + p0 + p) : 0;
+                const int st = p < n ? page_state(ids[p], int64_t(sg.y + p0 + p) * T, live_end) : 1;
+                if (st == 2 && lane == 0) atomicOr(a.error, kErrBadPage);
+                if (st == 0) mask |= 1u << p;
+            }
             if (lane == 0) {
                 const int ks = gs % KSS;
-                int ids[NP];
-                unsigned mask = 0;
-#pragma unroll
-                for (int p = 0; p < NP; ++p) {
-                    ids[p] = p < n ? __ldg(trow + p0 + p) : 0;
-                    const int st = p < n ? page_state(ids[p], int64_t(sg.y + p0 + p) * T, live_end) : 1;
-                    if (st == 2) atomicOr(a.error, kErrBadPage);
-                    if (st == 0) mask |= 1u << p;
-                }
                 if (!claim(kempty + ks, gs / KSS)) return;
                 const uint32_t fb = smem_u32(kfull + ks);
                 kvalid[ks] = mask;
@@ -219,24 +238,19 @@ __device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const 
                                         tm_k, 0, 0, b, g0.y, ids[p], fb);
                     }
             } else {
-                for (int p = 0; p < n; ++p) {
-                    const int jj = j + p, slot = jj % VS;
-                    const int id = __ldg(trow + p0 + p);
-                    const int st = page_state(id, int64_t(sg.y + p0 + p) * T, live_end);
-                    if (!claim(vempty + slot, jj / VS)) return;
-                    const uint32_t fb = smem_u32(vfull + slot);
-                    if (st != 0) {
-                        vvalid[slot] = 0;
-                        mbar_arrive(fb);
-                    } else {
-                        vvalid[slot] = 1;
-                        mbar_arrive_expect_tx(fb, HALF_BYTES);
-                        tma_load_5d(smem_u32(vring + size_t(slot) * HALF_BYTES), tm_v, 0, 0, 0, g0.y, id, fb);
-                    }
-                }
+                const int vs = gs % VSS;
+                if (!claim(vempty + vs, gs / VSS)) return;
+                const uint32_t fb = smem_u32(vfull + vs);
+                vvalid[vs] = mask;
+                if (mask) mbar_arrive_expect_tx(fb, uint32_t(__popc(mask)) * HALF_BYTES);
+                else mbar_arrive(fb);
+#pragma unroll
+                for (int p = 0; p < NP; ++p)
+                    if ((mask >> p) & 1u)
+                        tma_load_5d(smem_u32(vring + (size_t(vs) * NP + p) * HALF_BYTES), tm_v, 0, 0, 0, g0.y, ids[p],
+                                    fb);
             }
             ++gs;
-            j += n;
         }
     }
 }
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     paged_decode_mqa_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const DecodeArgs a) {
     using S = MqaShape<D, T>;
-    constexpr int NC = S::NC, NS = S::NS, NP = S::NP, KSS = S::KSS, VS = S::VS, GT = S::GT, OCW = S::OCW,
+    constexpr int NC = S::NC, NS = S::NS, NP = S::NP, KSS = S::KSS, VSS = S::VSS, GT = S::GT, OCW = S::OCW,
                   CW = S::CW, HALF = S::HALF_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -255,12 +269,12 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     uint8_t *qbuf = pbuf + 2 * S::P_BYTES;                  // [2][Q_BYTES]
     uint8_t *ring = qbuf + 2 * S::Q_BYTES;
     uint8_t *kring = ring;                                  // [KSS][box][NS tokens][128 B]
-    uint8_t *vring = ring + size_t(KSS) * S::KSTEP_BYTES;   // [VS][box][T tokens][128 B]
+    uint8_t *vring = ring + size_t(KSS) * S::KSTEP_BYTES;   // [VSS][NP pages][box][T tokens][128 B]
     uint64_t *kfull = reinterpret_cast<uint64_t *>(ring + S::RING);
     uint64_t *kempty = kfull + KSS;
     uint64_t *vfull = kempty + KSS;
-    uint64_t *vempty = vfull + VS;
-    uint64_t *s_full = vempty + VS;         // [2] per score block
+    uint64_t *vempty = vfull + VSS;
+    uint64_t *s_full = vempty + VSS;        // [2] per score block
     uint64_t *p_full = s_full + 2;          // [2] per weight buffer
     uint64_t *p_free = p_full + 2;          // [2]
     uint64_t *q_full = p_free + 2;          // [2] per query buffer
@@ -273,8 +287,8 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     float *xl = xmax + S::XMAX_BYTES / 4;
     unsigned *svalid = reinterpret_cast<unsigned *>(xl + S::XL_BYTES / 4);   // [2]: pages streamed, per score block
     unsigned *kvalid = svalid + 4;                                           // [KSS]: pages streamed, per K step
-    int *vvalid = reinterpret_cast<int *>(kvalid + KSS);
-    SmemFlags *flags = reinterpret_cast<SmemFlags *>(vvalid + VS);
+    unsigned *vvalid = kvalid + KSS;                                         // [VSS]: pages streamed, per V step
+    SmemFlags *flags = reinterpret_cast<SmemFlags *>(vvalid + VSS);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(flags + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -288,7 +302,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
             mbar_init(smem_u32(kfull + s), 1);
             mbar_init(smem_u32(kempty + s), 1);   // one commit of the score thread
         }
-        for (int s = 0; s < VS; ++s) {
+        for (int s = 0; s < VSS; ++s) {
             mbar_init(smem_u32(vfull + s), 1);
             mbar_init(smem_u32(vempty + s), 1);   // one commit of the PV thread
         }
@@ -327,7 +341,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
     const int xpar = int(xe & 1u);
 
     if (warp == NC) {
-        stream_mqa_pages<T, NP, NS, S::NBOX, HALF, S::KSTEP_BYTES, KSS, VS>(
+        stream_mqa_pages<T, NP, NS, S::NBOX, HALF, S::KSTEP_BYTES, KSS, VSS>(
             &tm_k, &tm_v, a, kring, vring, kfull, kempty, vfull, vempty, kvalid, vvalid, flags, seg_begin, seg_end,
             lane);
         if (a.pair) cluster_sync_all();   // the partner's merge waits for every thread of both CTAs
@@ -449,7 +463,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t ID_O = tc::idesc_f16_f32(S::M, D, false, true);    // P K-major, V MN-major
             bool stop = false;
-            int gs = 0, j = 0, sc = 0;
+            int gs = 0, sc = 0;
             for (int si = seg_begin; si < seg_end && !stop; ++si) {
                 const int4 sg = si == seg_begin ? sg_h : a.segs[si];
                 const int npg = sg.z - sg.y;
@@ -464,17 +478,17 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         stop = true;
                         break;
                     }
+                    const int vs = gs % VSS;
+                    if (!mbar_wait(smem_u32(vfull + vs), (gs / VSS) & 1)) {
+                        stop = true;
+                        break;
+                    }
                     tc::fence_after_sync();
                     const uint32_t pb = smem_u32(pbuf + b * S::P_BYTES);
+                    const unsigned vmask = vvalid[vs];
                     for (int p = 0; p < n; ++p) {
-                        const int jj = j + p;
-                        const int slot = jj % VS;
-                        if (!mbar_wait(smem_u32(vfull + slot), (jj / VS) & 1)) {
-                            stop = true;
-                            break;
-                        }
-                        if (!vvalid[slot]) continue;
-                        const uint32_t vb = smem_u32(vring + size_t(slot) * HALF);
+                        if (!((vmask >> p) & 1u)) continue;
+                        const uint32_t vb = smem_u32(vring + (size_t(vs) * NP + p) * HALF);
 #pragma unroll
                         for (int kk = 0; kk < S::PSTEPS; ++kk) {
                             const uint64_t ad =
@@ -484,11 +498,9 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                             accumulate = 1;
                         }
                     }
-                    if (stop) break;
                     tc::commit(smem_u32(p_free + b));
-                    for (int p = 0; p < n; ++p) tc::commit(smem_u32(vempty + (j + p) % VS));
+                    tc::commit(smem_u32(vempty + vs));
                     ++gs;
-                    j += n;
                 }
                 ++sc;
             }
@@ -572,7 +584,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                     rows = cluster_map(rows, prank ^ 1u);
                     ml = cluster_map(ml, prank ^ 1u);
                 }
-                if (mine) store_o_part<OCW>(rows + (lane & 15) * D, ov, oc0, half, f);
+                if (mine) store_pair_row<OCW>(rows + (lane & 15) * D, lane & 15, ov, oc0, half, f);
                 if (mine && cs == 0 && half == 0) ml[lane & 15] = make_float2(q.m_top, l);
                 return true;
             }
@@ -608,7 +620,7 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         Seg pend{};
         bool has_pend = false;
         int sc = 0;   // segments with pages so far: this one's output block is sc % 2
-        int gs = 0, j = 0;
+        int gs = 0;
         bool stop = false;
         for (int si = seg_begin; si < seg_end; ++si) {
             const int4 sg = si == seg_begin ? sg_h : a.segs[si];
@@ -714,11 +726,11 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         const int vt = (length - tok0) - pz * T;
                         if (length > tok0 && pz < n && vt > 0 && ((valid >> pz) & 1u)) {
                             // the page's load landed (seen here too, before writing over it)
-                            if (!warp_wait(vfull + (j + pz) % VS, ((j + pz) / VS) & 1)) {
+                            if (!warp_wait(vfull + gs % VSS, (gs / VSS) & 1)) {
                                 stop = true;
                                 break;
                             }
-                            uint8_t *vrows = vring + size_t((j + pz) % VS) * HALF;
+                            uint8_t *vrows = vring + (size_t(gs % VSS) * NP + pz) * HALF;
                             constexpr int UPR = S::NBOX * 8;   // 16-byte units per token row
                             for (int e = cs * 32 + lane; e < (T - vt) * UPR; e += 64) {
                                 const int row = vt + e / UPR, u16 = e % UPR;
@@ -761,7 +773,6 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         }
                     }
                     ++gs;
-                    j += n;
                 }
                 if (!stop) {
                     pend = Seg{sg, g0, nh, gs - 1, sc & 1, m_ref, m_top, l, o_live, true};
@@ -810,8 +821,9 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 16; e += 4) {
                         const int col = cs * (D / 2) + 32 * c + 16 * half + e;
-                        const float4 x = *reinterpret_cast<const float4 *>(ro + col);
-                        const float4 y = *reinterpret_cast<const float4 *>(rp + col);
+                        const int sw = 4 * ((col >> 2) ^ r);   // store_pair_row's chunk order
+                        const float4 x = *reinterpret_cast<const float4 *>(ro + sw);
+                        const float4 y = *reinterpret_cast<const float4 *>(rp + sw);
                         *reinterpret_cast<float4 *>(dst + col) =
                             make_float4(fmaf(x.x, so, y.x * sp), fmaf(x.y, so, y.y * sp), fmaf(x.z, so, y.z * sp),
                                         fmaf(x.w, so, y.w * sp));

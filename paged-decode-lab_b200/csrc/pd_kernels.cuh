@@ -93,7 +93,7 @@ KernelEntry entry_for_hg(int hg) {
 template <int D, int T>
 KernelEntry make_mqa_entry() {
     using S = MqaShape<D, T>;
-    return {&paged_decode_mqa_kernel<D, T>, S::THREADS, S::SMEM, S::NC, S::VS, 1};
+    return {&paged_decode_mqa_kernel<D, T>, S::THREADS, S::SMEM, S::NC, S::VSS * S::NP, 1};
 }
 
 template <typename Elt, int D, int T, int MODE>

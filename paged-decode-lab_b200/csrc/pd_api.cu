@@ -70,23 +70,39 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // of a page's rows for HG KV heads, landing in shared memory as
 // [head][128-byte box of the row][token] rows of 128 bytes, so the 128-byte
 // swizzle XORs by token and one instruction moves the whole K (or V) page.
-// With one_column the box is one 128-byte column of one head's page (T rows),
-// which the tcgen05 kernel places per column next to the step's other pages.
+// With token_groups (the tcgen05 kernel's K) the view splits the token into
+// 8-token groups, so that one box per page lands the rows of each 128-byte
+// column of a whole step at one fixed stride per 8 rows.
 pd_status encode_cache_map(const pd_plan &p, const void *base, pd_dtype dtype, int hg, CUtensorMap *map,
-                           bool one_column = false) {
+                           bool token_groups = false) {
     auto encode = tensor_map_encoder();
     if (!encode) return fail(PD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t elt = dtype == PD_FLOAT16 ? 2 : 4;
     const pd_layout &L = p.layout;
     const cuuint64_t row = cuuint64_t(L.head_dim) * elt;
+    const cuuint64_t nbox = row / 128;
+    const cuuint64_t hkv = cuuint64_t(L.kv_heads), T = cuuint64_t(L.page_size);
     // {128 bytes of a row, token, 128-byte box of the row, KV head, page}: one
     // box {all, T, all, hg, 1} lands as [head][box][token] 128-byte rows.
-    const cuuint64_t nbox = row / 128;
-    cuuint64_t dims[5] = {128 / elt, cuuint64_t(L.page_size), nbox, cuuint64_t(L.kv_heads),
-                          cuuint64_t(L.physical_pages)};
-    cuuint64_t strides[4] = {row * cuuint64_t(L.kv_heads), 128, row, row * cuuint64_t(L.kv_heads) * L.page_size};
-    cuuint32_t box[5] = {cuuint32_t(128 / elt), cuuint32_t(L.page_size), cuuint32_t(one_column ? 1 : nbox),
-                         cuuint32_t(hg), 1};
+    cuuint64_t dims[5] = {128 / elt, T, nbox, hkv, cuuint64_t(L.physical_pages)};
+    cuuint64_t strides[4] = {row * hkv, 128, row, row * hkv * T};
+    cuuint32_t box[5] = {cuuint32_t(128 / elt), cuuint32_t(T), cuuint32_t(nbox), cuuint32_t(hg), 1};
+    if (token_groups) {
+        // The tcgen05 kernel's K: {128 bytes, token within 8, 128-byte box of
+        // any KV head's row (box b of head h is h * nbox + b), 8-token group,
+        // page}; one box {all, 8, nbox, T / 8, 1} per page and head lands as
+        // [group][box][8 tokens] 128-byte rows, so the 8-row groups of one box
+        // column sit nbox * 1024 bytes apart across all pages of a step.
+        dims[1] = 8;
+        dims[2] = nbox * hkv;
+        dims[3] = T / 8;
+        strides[0] = row * hkv;
+        strides[1] = 128;
+        strides[2] = 8 * row * hkv;
+        box[1] = 8;
+        box[3] = cuuint32_t(T / 8);
+        box[4] = 1;
+    }
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = encode(map,
                               dtype == PD_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -176,16 +192,16 @@ pd_status launch(pd_plan *p, const void *k, const void *v, pd_dtype dtype, int m
     if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
         return fail(PD_ERR_VALUE, "k and v must be 16-byte aligned");
     TensorMapCache &tc = p->tmaps;
-    const int one_column = p->engine == kEngineTensorMemory && mode == kModeDecode ? 1 : 0;
-    if (tc.k != k || tc.v != v || tc.dtype != int(dtype) || tc.one_column != one_column) {
-        pd_status s = encode_cache_map(*p, k, dtype, p->heads_per_tile, &tc.map_k, one_column != 0);
+    const int token_groups = p->engine == kEngineTensorMemory && mode == kModeDecode ? 1 : 0;
+    if (tc.k != k || tc.v != v || tc.dtype != int(dtype) || tc.token_groups != token_groups) {
+        pd_status s = encode_cache_map(*p, k, dtype, p->heads_per_tile, &tc.map_k, token_groups != 0);
         if (s != PD_OK) return s;
         s = encode_cache_map(*p, v, dtype, p->heads_per_tile, &tc.map_v);
         if (s != PD_OK) return s;
         tc.k = k;
         tc.v = v;
         tc.dtype = int(dtype);
-        tc.one_column = one_column;
+        tc.token_groups = token_groups;
     }
     const KernelEntry e =
         kernel_for(dtype, p->layout.head_dim, p->layout.page_size, p->group_tile, p->heads_per_tile, mode,

@@ -8,8 +8,10 @@
 // segment (NS = NP * T = 128 score columns):
 //
 //   * warp 7 (producer): lane 0 streams K a step at a time into step slots
-//     laid out [128-byte column][NS tokens][128 B], lane 1 each page's V into
-//     page slots; the lanes walk the work list independently;
+//     laid out [page][8-token group][128-byte column][8 tokens][128 B] (one
+//     8 KiB box per page: a column's 8-row groups sit a fixed stride apart over
+//     the whole step), lane 1 a step's V pages into V step slots; the lanes
+//     walk the work list independently;
 //   * warp 2 stages each segment's 32 query rows in shared memory (128-byte
 //     swizzled, K-major) two segments ahead;
 //   * one thread of warp 3 issues S = Q K^T for a whole step once its K has
@@ -88,8 +90,9 @@ struct MqaShape {
     static constexpr int XMAX_BYTES = 2 * 2 * 2 * 16 * 4;   // [pair phase][heads half][warp][row] row maxima
     static constexpr int XL_BYTES = 2 * 2 * 16 * 4;         // [heads half][warp][row] denominators
     static constexpr int PAIR_ML_BYTES = 2 * 16 * 8;        // pair plans: (m, l) of 16 rows, own and received
-    // K arrives a step at a time into KSS step slots laid out [box][NS tokens]
-    // [128 B], so one MMA takes a whole step's scores per 16 head dims; a step
+    // K arrives a step at a time into KSS step slots laid out [page][8-token
+    // group][box][8 tokens][128 B], so one MMA takes a whole step's scores per
+    // 16 head dims (its 8-row groups NBOX * 1024 bytes apart); a step
     // slot is free once those scores are done.  V also arrives a step at a time
     // (its NP pages on one mbarrier, [page][box][T tokens][128 B]) into VSS
     // step slots, each free once its PV products are done; the V ring holds two
@@ -168,8 +171,8 @@ __device__ __forceinline__ float ex2_ftz(float x) {
 // Producer warp of the tcgen05 kernel: two lanes, each walking the CTA's work
 // list on its own, so that neither kind of load waits for the other's slots.
 //   lane 0, K by steps (NP consecutive pages of one segment): step s into step
-//     slot s % KSS, one TMA load per page and 128-byte column (page p, column b
-//     at b * NS * 128 + p * T * 128), once the scores of step s - KSS are done;
+//     slot s % KSS, one TMA load per page (the token-group view: page p at
+//     p * HALF_BYTES), once the scores of step s - KSS are done;
 //   lane 1, V by steps: step s into V step slot s % VSS, one TMA load per
 //     page ([column][token], page p at p * HALF_BYTES), once the PV products
 //     of step s - VSS are done.
@@ -231,12 +234,9 @@ __device__ __forceinline__ void stream_mqa_pages(const CUtensorMap *tm_k, const 
                 else mbar_arrive(fb);
 #pragma unroll
                 for (int p = 0; p < NP; ++p)
-                    if ((mask >> p) & 1u) {
-#pragma unroll
-                        for (int b = 0; b < NBOX; ++b)
-                            tma_load_5d(smem_u32(kring + size_t(ks) * KSTEP_BYTES + b * (NS * 128) + p * (T * 128)),
-                                        tm_k, 0, 0, b, g0.y, ids[p], fb);
-                    }
+                    if ((mask >> p) & 1u)
+                        tma_load_5d(smem_u32(kring + size_t(ks) * KSTEP_BYTES + p * HALF_BYTES), tm_k, 0, 0,
+                                    g0.y * NBOX, 0, ids[p], fb);
             } else {
                 const int vs = gs % VSS;
                 if (!claim(vempty + vs, gs / VSS)) return;
@@ -432,10 +432,10 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
                         const uint32_t kb = smem_u32(kring + size_t(ks) * S::KSTEP_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < S::KSTEPS; ++kk) {
-                            const uint32_t koff = (kk >> 2) * (NS * 128) + (kk & 3) * 32;
+                            const uint32_t koff = (kk >> 2) * 1024 + (kk & 3) * 32;
                             const uint64_t ad = tc::smem_desc(qa + (kk >> 2) * S::Q_BOX + (kk & 3) * 32, 16, 1024,
                                                               tc::kSwizzle128);
-                            const uint64_t bd = tc::smem_desc(kb + koff, 16, 1024, tc::kSwizzle128);
+                            const uint64_t bd = tc::smem_desc(kb + koff, 16, S::NBOX * 1024, tc::kSwizzle128);
                             tc::mma_f16(tmem + S::S_COL + b * NS, ad, bd, ID_S, kk > 0 ? 1u : 0u);
                         }
                     }

@@ -29,7 +29,7 @@ struct TensorMapCache {
     const void *k = nullptr;
     const void *v = nullptr;
     int dtype = -1;
-    int one_column = -1;   // map_k loads one 128-byte column per box (the tcgen05 kernel's decode)
+    int token_groups = -1;   // map_k lands pages as [8-token group][box][8 tokens] (the tcgen05 kernel's decode)
     alignas(64) CUtensorMap map_k;
     alignas(64) CUtensorMap map_v;
 };

@@ -73,7 +73,7 @@ NCU_TRAFFIC_BYTES = {"c1": 67_258_880 + 571_648, "c2": 469_731_072 + 5_400_320,
 NCU_TRAFFIC_BYTES["c4s"] = 580_584_448 + 4_443_648
 NCU_SCALED = {"c4": ("c4s", NCU_TRAFFIC_BYTES["c4s"])}   # workload -> (captured workload, its traffic)
 # the same for plans on the tcgen05 kernel (paged_decode_mqa_kernel)
-NCU_TRAFFIC_BYTES_TCGEN05 = {"c3b": 67_816_960 + 1_204_992}
+NCU_TRAFFIC_BYTES_TCGEN05 = {"c3b": 67_764_736 + 709_120}
 
 
 def parse_args():

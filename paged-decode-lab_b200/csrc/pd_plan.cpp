@@ -134,16 +134,15 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
         if (kib >= 1) target = kib * 1024;
     }
     // FP16 group tiles of 32 query heads: the tcgen05 kernel (one KV head per
-    // page tile) where it measured faster than the warp-level kernel (m16n8k16
-    // MMAs, up to two KV heads per tile): head_dim 128 with 32-token pages
-    // (config 3b 24.8 against 25.4 us).  With 16-token pages it is slower (its
-    // steps carry twice the loads and PV products per byte).  PD_MQA_ENGINE=
-    // tcgen05 or warp forces either kernel for every such plan.
+    // page tile), measured faster than the warp-level kernel (m16n8k16 MMAs,
+    // up to two KV heads per tile) for head_dim 64 and 128 with pages of 16
+    // and 32 tokens (B64 x 2048 tokens, 32:1: 15.1 / 20.4 us against 19.1 /
+    // 22.0 at head_dim 64, 17.5 / 21.1 against 25.3 / 30.3 at head_dim 128,
+    // pages 32 / 16; eight sequences of 8k tokens: 18.9 against 18.1).
+    // PD_MQA_ENGINE=tcgen05 or warp forces either kernel for every such plan.
     const char *engine_env = std::getenv("PD_MQA_ENGINE");
-    const bool force_tc = engine_env && std::strcmp(engine_env, "tcgen05") == 0;
     const bool force_warp = engine_env && std::strcmp(engine_env, "warp") == 0;
-    const bool tensor_memory = dtype == PD_FLOAT16 && p.group_tile == 32 && !force_warp &&
-                               (force_tc || (L.head_dim == 128 && T == 32));
+    const bool tensor_memory = dtype == PD_FLOAT16 && p.group_tile == 32 && !force_warp;
     const int hg = tensor_memory ? 1
                                  : choose_heads_per_tile(dtype == PD_FLOAT16 ? 2 : 4, L.head_dim, T, p.group_tile,
                                                          L.kv_heads, target);

@@ -2,8 +2,8 @@
 
 FP16 plans whose group tile holds 32 query heads run on the kernel that issues
 its QK^T and PV products from single threads into tensor memory
-(csrc/pd_decode_mqa.cuh) by default for head_dim 128 with 32-token pages, and
-for every such shape with PD_MQA_ENGINE=tcgen05.  The CPU tests pin the planner's choice (engine,
+(csrc/pd_decode_mqa.cuh) by default (PD_MQA_ENGINE=warp keeps them on the
+warp-level kernel).  The CPU tests pin the planner's choice (engine,
 one KV head per page tile, one partial slot per segment).  The GPU tests check
 that kernel against the FP64 oracle on the shapes it serves (head_dim 64 and
 128, pages of 16 and 32 tokens, groups of 17, 24, 32 and 64 query heads per
@@ -53,16 +53,17 @@ def test_fp16_group_tiles_of_32_heads_choose_the_tcgen05_kernel(heads, kv_heads,
 
 
 def test_default_engine_and_overrides(monkeypatch):
-    """By default the tcgen05 kernel takes head_dim 128 with 32-token pages
-    (where it measured faster); PD_MQA_ENGINE=warp or tcgen05 forces a kernel."""
+    """By default the tcgen05 kernel takes every FP16 group tile of 32 query
+    heads (head_dim 64 or 128, pages of 16 or 32 tokens: measured faster);
+    PD_MQA_ENGINE=warp keeps such plans on the warp-level kernel."""
     monkeypatch.delenv("PD_MQA_ENGINE", raising=False)
     layout, table, lengths = _fragmented(2, 32, 1, 128, 32, [500, 70])
     assert inspect_plan(layout, table, lengths)["info"]["engine"] == TCGEN05
     for dim, page in ((128, 16), (64, 32), (64, 16)):
         small = _fragmented(2, 32, 1, dim, page, [500, 70])
-        assert inspect_plan(*small)["info"]["engine"] == 0
-        monkeypatch.setenv("PD_MQA_ENGINE", "tcgen05")
         assert inspect_plan(*small)["info"]["engine"] == TCGEN05
+        monkeypatch.setenv("PD_MQA_ENGINE", "warp")
+        assert inspect_plan(*small)["info"]["engine"] == 0
         monkeypatch.delenv("PD_MQA_ENGINE")
     monkeypatch.setenv("PD_MQA_ENGINE", "warp")
     info = inspect_plan(layout, table, lengths)["info"]

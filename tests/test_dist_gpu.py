@@ -43,9 +43,14 @@ def _worker(rank, world, port, q_out, mode):
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        # "_mqa" modes: 32 query heads on one KV head, the tcgen05 kernel's shape
-        kv_heads = 1 if mode.endswith("_mqa") else 8
-        layout, table, lengths = make_metadata(3, 32, kv_heads, 128, 3000, 32, seed=5)
+        # "_mqa" modes: 32 query heads on one KV head, the tcgen05 kernel's shape;
+        # "_pair": 64 equal sequences, so each rank's plan pairs CTAs in clusters
+        kv_heads = 1 if mode.endswith("_mqa") or mode.endswith("_pair") else 8
+        batch = 64 if mode.endswith("_pair") else 3
+        if mode.endswith("_pair"):
+            layout, table, lengths = make_metadata(batch, 32, 1, 128, 1024, 32, seed=5, ragged=False)
+        else:
+            layout, table, lengths = make_metadata(batch, 32, kv_heads, 128, 3000, 32, seed=5)
         q, k, v = make_tensors(layout, device=f"cuda:{rank}", seed=6)
         if mode == "kv_head":
             plan = pd_dist.KVHeadShardedPlan(layout, table, lengths, rank=rank, world=world,
@@ -56,13 +61,15 @@ def _worker(rank, world, port, q_out, mode):
         else:
             lt, ll, _ = pd_dist.shard_sequence_metadata(table, lengths, 32, rank, world)
             ltab, ids = pd_dist.localize_pages(lt, ll, 32)
-            loc = Layout(3, 32, kv_heads, 128, 32, max(1, len(ids)))
+            loc = Layout(batch, 32, kv_heads, 128, 32, max(1, len(ids)))
             idx = torch.as_tensor(ids, device=q.device)
             kl, vl = k[idx].contiguous(), v[idx].contiguous()
             exchange = "peer" if mode.startswith("sequence_peer") else "nccl"
             plan = pd_dist.SequenceShardedPlan(loc, ltab, ll, device=f"cuda:{rank}", exchange=exchange)
-            if mode.endswith("_mqa"):
+            if mode.endswith("_mqa") or mode.endswith("_pair"):
                 assert plan.plan.info.engine == 1   # the tcgen05 kernel
+            if mode.endswith("_pair"):
+                assert plan.plan.info.cluster_ctas == 2   # (m, l) of pair plans feed the NCCL merge
             first = plan.run(q, kl, vl).clone()
             for _ in range(7):      # alternate exchange parities; every step the same bits
                 again = plan.run(q, kl, vl)
@@ -82,7 +89,8 @@ def _worker(rank, world, port, q_out, mode):
         q_out.put((rank, False, f"{type(exc).__name__}: {exc}"))
 
 
-@pytest.mark.parametrize("mode", ["kv_head", "sequence", "sequence_peer", "sequence_mqa", "sequence_peer_mqa"])
+@pytest.mark.parametrize("mode", ["kv_head", "sequence", "sequence_peer", "sequence_mqa", "sequence_peer_mqa",
+                                  "sequence_pair"])
 def test_two_gpu_sharding_matches_oracle(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

@@ -138,6 +138,25 @@ def test_static_runs_a_plan_that_was_never_bound(dtype):
     assert plan.lib.pd_plan_read_errors(plan.handle, ctypes.byref(word), _stream()) == _native.PD_ERR_UNBOUND
 
 
+def test_static_runs_a_pair_plan():
+    # 64 equal MQA sequences: a pair plan (clusters of two CTAs that merge each
+    # group in shared memory, no partials) through the static entry point
+    layout, table, lengths = make_metadata(64, 32, 1, 128, 512, 32, seed=44, ragged=False)
+    q, k, v = make_tensors(layout, seed=45)
+    plan = UnboundPlan(layout, table, lengths, torch.float16, num_ctas=0)
+    assert plan.info.cluster_ctas == 2 and plan.info.num_pieces == 0
+    bound = DecodePlan(layout, table, lengths)
+    assert bound.info.cluster_ctas == 2
+    ref = bound.run(q, k, v).cpu().numpy()
+    np.testing.assert_allclose(ref, _oracle(q, k, v, table, lengths), **TOL[torch.float16])
+    for _ in range(2):
+        out = torch.full((64, 32, 128), float("nan"), device=q.device)
+        _native.check(_static(plan.handle, q, k, v, out))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), ref)   # the same work split: the same bits
+        assert _static_errors() == 0
+
+
 def test_static_alternating_plans_on_one_stream():
     # A (partials, in-kernel merge), B (no partials), A again: each call
     # overwrites the array the previous one used, with no synchronisation between

@@ -280,3 +280,28 @@ def test_exchange_rejects_pair_plans():
                                     v.data_ptr(), _native.PD_FLOAT16, ptrs, 0, 1, out.data_ptr(), None, stream)
     assert status == _native.PD_ERR_VALUE
     assert b"CTA pairs" in lib.pd_last_error()
+
+
+@pytest.mark.gpu
+def test_gather_on_a_pair_plan_is_bit_exact_and_decode_repeats():
+    # the gather debug mode walks a pair plan's two segments per group on the
+    # warp-level kernel (no cluster); decodes before and after it (the K tensor
+    # map switches between the page view and the token-group view) agree bit for bit
+    torch = _torch()
+    from oracle.paged_oracle import gather_cache
+    from paged_decode.workload import make_tensors
+    layout, table, lengths = _uniform(64, 32, 1, 128, 32, 200, seed=17)
+    q, k, v = make_tensors(layout, seed=18)
+    plan = _plan(layout, table, lengths, pair=None, engine=None)
+    assert plan.info.cluster_ctas == 2
+    before = plan.run(q, k, v).clone()
+    dense_k, dense_v = plan.gather(k, v)
+    after = plan.run(q, k, v)
+    assert torch.equal(before, after)
+    dk, dv = dense_k.cpu().numpy(), dense_v.cpu().numpy()
+    kc, vc = k.cpu().numpy(), v.cpu().numpy()
+    for b in range(layout.batch):
+        n = int(lengths[b])
+        np.testing.assert_array_equal(dk[b, 0, :n].astype(np.float64), gather_cache(kc, table[b], n, 0))
+        np.testing.assert_array_equal(dv[b, 0, :n].astype(np.float64), gather_cache(vc, table[b], n, 0))
+    assert plan.read_errors() == 0

@@ -17,10 +17,10 @@
 //   * one thread of warp 3 issues S = Q K^T for a whole step once its K has
 //     landed (M = 64 rows of which the 32 query heads are 0..31, N = NS, K =
 //     16 head dims per MMA) into one of two score blocks in tensor memory;
-//     one thread of warp 6, once a step's weights P are in shared memory,
-//     issues O += P V page by page as V lands (N = head dim) into one of two
-//     output blocks (consecutive segments alternate).  Two issuing threads,
-//     so that neither kind waits for the other's inputs;
+//     one thread of warp 6, once a step's weights P are in shared memory and
+//     its V pages have landed, issues O += P V page by page (N = head dim)
+//     into one of two output blocks (consecutive segments alternate).  Two
+//     issuing threads, so that neither kind waits for the other's inputs;
 //   * warps 0 and 4 own query heads 0..15, warps 1 and 5 heads 16..31
 //     (tensor-memory lanes 0..15 of sub-partitions 0 and 1); of each step's
 //     columns a warp takes one half, two threads per head.  Online softmax in
@@ -456,10 +456,10 @@ __global__ void __launch_bounds__(MqaShape<D, T>::THREADS, 1)
         __syncwarp();
     } else if (warp == S::W_PV) {
         // ------------------------------------------------------------ PV MMAs (one thread)
-        // Once a step's weights are written: O += P V for each page as its V
-        // lands (a segment's first product overwrites, after the previous
-        // segment's output block was read back), then commits that free the
-        // weight buffer and the step's V pages.
+        // Once a step's weights are written and its V step has landed: O += P V
+        // for each streamed page (a segment's first product overwrites, after
+        // the previous segment's output block was read back), then commits that
+        // free the weight buffer and the V step slot.
         if (lane == 0) {
             constexpr uint32_t ID_O = tc::idesc_f16_f32(S::M, D, false, true);    // P K-major, V MN-major
             bool stop = false;

@@ -500,7 +500,7 @@ PD_API pd_status pd_merge_shards(const float *shard_out, const float *shard_stat
 namespace pd {
 namespace {
 constexpr size_t kStaticScratchBytes = size_t(16) << 20;
-__device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_static_mutex;
 constexpr int kMaxDevices = 256;

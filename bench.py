@@ -672,7 +672,8 @@ def run_ours(args, rank, local, world):
                    "sharding": job.sharding, "l2": l2, "timing": how,
                    "persistent_ctas": int(info.num_ctas),
                    "kv_heads_per_tile": int(info.heads_per_tile),
-                   "engine": "tcgen05" if tcgen05 else "warp"},
+                   "engine": "tcgen05" if tcgen05 else "warp",
+                   "cluster_ctas": int(info.cluster_ctas)},
         "windows": {"count": args.windows, "steps_each": args.steps,
                     "median_us": step_ms * 1e3, "min_us": min(window_ms) * 1e3,
                     "p95_us": percentile(window_ms, 95) * 1e3,

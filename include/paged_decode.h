@@ -94,7 +94,8 @@ typedef struct pd_plan_info {
     int32_t cluster_ctas;    /* CTAs per thread-block cluster of the decode launch: 1, or 2 for a
                                 pair plan (tcgen05 engine, num_ctas <= 0 at creation, groups of
                                 near-equal length that fill at least 3/4 of the SMs two CTAs
-                                each; PD_PAIR=0 / 1 in the environment at plan creation turns
+                                each, and on a device only if all its clusters fit at once;
+                                PD_PAIR=0 / 1 in the environment at plan creation turns
                                 it off / on wherever the groups fit): the two CTAs of a cluster
                                 stream the two halves of one group and merge them through
                                 distributed shared memory, with no partials, grid barrier or

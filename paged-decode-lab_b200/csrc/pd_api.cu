@@ -320,6 +320,32 @@ int64_t exchange_slot_bytes(const pd_plan *p) {
 using namespace pd;
 
 namespace {
+// Clusters of two CTAs of a pair plan's decode kernel that can be resident at once on `device`.
+pd_status max_active_pair_clusters(const pd_plan &p, int device, int *clusters) {
+    const KernelEntry e = kernel_for(p.dtype, p.layout.head_dim, p.layout.page_size, p.group_tile,
+                                     p.heads_per_tile, kModeDecode, p.engine);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(guard.err));
+    pd_status s = ensure_smem_attribute(device, e);
+    if (s != PD_OK) return s;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(p.num_ctas));
+    cfg.blockDim = dim3(unsigned(e.threads));
+    cfg.dynamicSmemBytes = e.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaOccupancyMaxActiveClusters(clusters, e.fn, &cfg);
+    if (err != cudaSuccess)
+        return fail(PD_ERR_CUDA, std::string("cluster occupancy query: ") + cudaGetErrorString(err));
+    return PD_OK;
+}
+
 pd_status create_impl(const pd_layout *layout, const int32_t *table, int64_t table_width,
                       const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
                       int32_t merge_mode, pd_dtype dtype, int32_t device, int32_t num_ctas,
@@ -334,8 +360,19 @@ pd_status create_impl(const pd_layout *layout, const int32_t *table, int64_t tab
     }
     pd_plan *p = new (std::nothrow) pd_plan();
     if (!p) return fail(PD_ERR_VALUE, "out of host memory");
-    const pd_status s = build_plan(layout, table, table_width, lengths, max_lengths, split_tokens, merge_mode,
-                                   dtype, num_ctas, sm_count, *p);
+    pd_status s = build_plan(layout, table, table_width, lengths, max_lengths, split_tokens, merge_mode,
+                             dtype, num_ctas, sm_count, *p);
+    if (s == PD_OK && p->cluster == 2 && device >= 0) {
+        // A pair plan only where all its clusters of two CTAs fit on the device
+        // at once (shared memory, GPC boundaries); otherwise one CTA per SM.
+        int clusters = 0;
+        s = max_active_pair_clusters(*p, device, &clusters);
+        if (s == PD_OK && 2 * int64_t(clusters) < p->num_ctas) {
+            *p = pd_plan();
+            s = build_plan(layout, table, table_width, lengths, max_lengths, split_tokens, merge_mode, dtype,
+                           num_ctas, sm_count, *p, false);
+        }
+    }
     if (s != PD_OK) {
         delete p;
         return s;

@@ -45,7 +45,7 @@ const std::string &last_error() { return g_last_error; }
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
                      const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
                      int32_t merge_mode, pd_dtype dtype, int32_t num_ctas, int32_t sm_count,
-                     pd_plan &p) {
+                     pd_plan &p, bool allow_pair) {
     if (!layout) return fail(PD_ERR_VALUE, "layout must not be NULL");
     const pd_layout L = *layout;
     // Layout.__post_init__ (oracle.py:24-27)
@@ -188,7 +188,7 @@ pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t widt
     // no partials, no grid barrier, no merge kernel.  PD_PAIR=0 / 1 turns
     // the choice off / on wherever the groups fit.
     p.cluster = 1;
-    if (p.engine == kEngineTensorMemory && num_ctas <= 0 && sm_count > 0 && ngroups >= 1 &&
+    if (allow_pair && p.engine == kEngineTensorMemory && num_ctas <= 0 && sm_count > 0 && ngroups >= 1 &&
         2 * ngroups <= std::min(sm_count, 1024)) {
         int64_t longest = 0;
         for (int64_t gi = 0; gi < ngroups; ++gi) longest = std::max(longest, gpages[gi]);

@@ -84,9 +84,10 @@ namespace pd {
 // `max_lengths` (nullable) makes a dynamic plan: its work list covers
 // sequence b up to max_lengths[b] tokens, and launches may pass live lengths
 // <= max_lengths and a page table updated on the device.
+// `allow_pair` = false never builds a pair plan (clusters of two CTAs).
 pd_status build_plan(const pd_layout *layout, const int32_t *table, int64_t width,
                      const int32_t *lengths, const int32_t *max_lengths, int32_t split_tokens,
                      int32_t merge_mode, pd_dtype dtype, int32_t num_ctas, int32_t sm_count,
-                     pd_plan &plan);
+                     pd_plan &plan, bool allow_pair = true);
 
 }  // namespace pd

@@ -305,3 +305,25 @@ def test_gather_on_a_pair_plan_is_bit_exact_and_decode_repeats():
         np.testing.assert_array_equal(dk[b, 0, :n].astype(np.float64), gather_cache(kc, table[b], n, 0))
         np.testing.assert_array_equal(dv[b, 0, :n].astype(np.float64), gather_cache(vc, table[b], n, 0))
     assert plan.read_errors() == 0
+
+
+@pytest.mark.gpu
+def test_pair_plans_only_where_all_clusters_fit_at_once():
+    # as many groups as half the SMs: a pair plan only if the device holds that
+    # many clusters of two CTAs at once (otherwise a cluster would wait for a
+    # second wave), else one CTA per SM; the output is right either way
+    torch = _torch()
+    from paged_decode.workload import make_tensors
+    groups = torch.cuda.get_device_properties(0).multi_processor_count // 2
+    layout, table, lengths = _uniform(groups, 32, 1, 128, 32, 512, seed=19)
+    q, k, v = make_tensors(layout, seed=20)
+    plan = _plan(layout, table, lengths, pair="1", engine=None)
+    print(f"{groups} groups: cluster_ctas {plan.info.cluster_ctas}, num_ctas {plan.num_ctas}")
+    if plan.info.cluster_ctas == 2:
+        assert plan.num_ctas == 2 * groups
+    out = plan.run(q, k, v).cpu().numpy()
+    np.testing.assert_allclose(out, _oracle(q, k, v, table, lengths), **TOL)
+    assert plan.read_errors() == 0
+    # config 3b's 64 groups stay a pair plan
+    layout, table, lengths = _uniform(64, 32, 1, 128, 32, 512, seed=21)
+    assert _plan(layout, table, lengths, pair=None, engine=None).info.cluster_ctas == 2
